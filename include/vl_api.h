@@ -1,0 +1,270 @@
+/*
+ * vl_api.h - C ABI of libvlasr.so, the sm_100a (B200) implementation of the
+ * memory-bound layer ops of the GLM-ASR native engine:
+ *
+ *   log-mel frontend, residual-add + LayerNorm, residual-add + RMSNorm,
+ *   exact-erf GELU (optionally with a fused bias add), SwiGLU, rotary
+ *   embedding on Q/K in place, token-embedding gather and KV-cache append.
+ *
+ * Reference interfaces replaced (paths inside the VideoLingo-user project):
+ *   native/asr/src/mel_frontend.h:26-32   compute_mel / compute_mel_batched
+ *   native/asr/src/engine.cu:162-233      layer_norm / gelu / add_bias /
+ *                                         residual_add / rope kernels
+ *   native/asr/src/decoder.cu:60-134,307-351,460-514,636-695,789-814,
+ *                            857-882,933-948
+ *                                         embedding gathers, rmsnorm,
+ *                                         silu_mul, RoPE and KV-append kernels
+ * In the reference those ops are anonymous-namespace __global__ functions
+ * launched by the engine's host code with compile-time shapes; this header is
+ * the stable, shape-parameterised boundary a host (Python via ctypes, C, C++)
+ * binds instead.
+ *
+ * Conventions shared by every entry point
+ *   - Return value: VL_OK (0) on success, VL_ERR_EXEC (1) when a CUDA launch
+ *     fails, VL_ERR_INVALID (2) for an invalid argument.  These mirror the
+ *     reference CLI's exit codes (native/asr/src/main_m0.cu:6-7,696-703:
+ *     0 ok, 1 ModelExecutionError, 2 ModelInputError).  vl_last_error()
+ *     returns the message of the last failure on the calling thread.
+ *   - Invalid arguments are detected on the host before any CUDA call, so a
+ *     rejected call has no side effects and needs no GPU.
+ *   - Buffers are caller-owned DEVICE pointers; ops never allocate, never
+ *     synchronise and run on the caller's stream (`stream` is a cudaStream_t
+ *     passed as void*; NULL = the legacy default stream).
+ *   - Ops are stateless and thread-safe; launches on one stream are ordered.
+ *   - Float ops compute in fp32 and round once to the storage type (RNE);
+ *     the rounding points are those of the reference kernels (documented per
+ *     op below).  Index ops (gather, KV append) are bit-exact copies.
+ *   - Index values that live in device memory (token ids, slots, audio
+ *     placeholder counts) cannot be checked on the host.  The kernels never
+ *     access memory out of bounds: an offending row is zero-filled (gather)
+ *     or skipped (KV append) and, when `status` is non-NULL, a bit is OR-ed
+ *     into *status (a device int32 the caller zeroes and later reads).
+ */
+#ifndef VL_API_H_
+#define VL_API_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VL_EXPORT __attribute__((visibility("default")))
+#else
+#define VL_EXPORT
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define VL_OK 0
+#define VL_ERR_EXEC 1
+#define VL_ERR_INVALID 2
+
+/* Element types of activation tensors. */
+#define VL_F32 0
+#define VL_F16 1
+#define VL_BF16 2
+
+/* Bits OR-ed into a device-side *status word by the index ops. */
+#define VL_STATUS_BAD_ID 1      /* token id outside [0, vocab)              */
+#define VL_STATUS_BAD_AUDIO 2   /* more audio placeholders than audio rows  */
+#define VL_STATUS_BAD_SLOT 4    /* KV slot >= num_slots                      */
+
+/* Whisper/GLM-ASR log-mel geometry (native/asr/src/mel_frontend.h:34-42). */
+#define VL_MEL_BINS 128
+#define VL_MEL_FFT 400
+#define VL_MEL_HOP 160
+#define VL_MEL_CHUNK_SAMPLES 480000
+#define VL_MEL_FRAMES 3000
+
+/* Library version (major*10000 + minor*100 + patch). */
+VL_EXPORT int vl_version(void);
+
+/* Message of the last failed call on this thread ("" when none). */
+VL_EXPORT const char* vl_last_error(void);
+
+/* Number of CUDA devices visible to the library (0 on a host without GPU). */
+VL_EXPORT int vl_device_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* Log-mel frontend                                                          */
+/* ------------------------------------------------------------------------ */
+
+/* Workspace bytes vl_logmel needs for `chunks` chunks (per-tile maxima). */
+VL_EXPORT size_t vl_logmel_workspace_bytes(int64_t chunks);
+
+/*
+ * Whisper log-mel features of `chunks` independent 30 s chunks.
+ * Replaces compute_mel_batched (native/asr/src/mel_frontend.cu:209-291;
+ * declared native/asr/src/mel_frontend.h:30-32).
+ *
+ *   pcm  [chunks][480000] f32, 16 kHz mono, already zero-padded per chunk
+ *        (the reference throws unless size == chunks*480000).
+ *   out  [chunks][128][3000] f32.
+ *
+ * Per chunk: reflect pad 200, periodic Hann, |rfft_400|^2 on hop-160 frames,
+ * 128-bin Slaney mel filterbank (0-8000 Hz), log10(max(x,1e-10)) over
+ * frames 0..2999 (the 3001st frame is dropped), clamp to (chunk max - 8),
+ * then (x+4)/4.  pcm and out must be 16-byte aligned; workspace must hold
+ * vl_logmel_workspace_bytes(chunks) bytes (16-byte aligned) and needs no
+ * initialisation.  `out` must not overlap `pcm`.
+ */
+VL_EXPORT int vl_logmel(const float* pcm, int64_t chunks, float* out, void* workspace,
+              size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Norms                                                                     */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Residual add + LayerNorm over the last dimension (rows x cols, row-major,
+ * contiguous).  Replaces residual_add_kernel -> cudaMemcpy -> layer_norm_kernel
+ * (native/asr/src/engine.cu:207-212, :162-192, sequence :1544-1552).
+ *
+ *   delta != NULL:  h = round(residual + delta); residual := h;
+ *                   out = round((h - mean) * rsqrt(var + eps) * gamma + beta)
+ *   delta == NULL:  out = LayerNorm(residual); residual is only read
+ *                   (out == residual gives the reference's in-place LN).
+ * mean = sum(h)/cols and var = sum(h^2)/cols - mean^2 in fp32, computed from
+ * the ROUNDED h exactly as the reference normalises the stored half value;
+ * var is clamped at 0 (the reference would produce NaN on a degenerate row).
+ * `out` may alias `delta`; with delta != NULL it must not alias `residual`.
+ * gamma/beta are [cols] of the same dtype; beta may be NULL (no bias).
+ */
+VL_EXPORT int vl_add_layernorm(void* residual, const void* delta, const void* gamma,
+                     const void* beta, void* out, int64_t rows, int64_t cols,
+                     float eps, int dtype, void* stream);
+
+/*
+ * Residual add + RMSNorm.  Replaces residual_add_kernel -> cudaMemcpy ->
+ * rmsnorm_kernel (native/asr/src/decoder.cu:933-938, :81-101, sequence
+ * :1591-1597 and :1727-1733).
+ *   h as above; out = round((h * rsqrt(sum(h^2)/cols + eps)) * weight).
+ * Same aliasing rules as vl_add_layernorm.
+ */
+VL_EXPORT int vl_add_rmsnorm(void* residual, const void* delta, const void* weight,
+                   void* out, int64_t rows, int64_t cols, float eps, int dtype,
+                   void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Activations                                                               */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Exact-erf GELU, optionally after a bias add.  Replaces add_bias_kernel +
+ * gelu_kernel (native/asr/src/engine.cu:200-205, :194-198, gelu :110-112).
+ *   bias == NULL:  out = round(0.5*x*(1+erf(x/sqrt(2))))
+ *   bias != NULL:  t = round(x + bias[col]); out = round(gelu(t))
+ *                  (the reference stores the biased value before GELU).
+ * in/out are rows x cols contiguous; out may equal in (in place).
+ */
+VL_EXPORT int vl_gelu_erf(const void* in, const void* bias, void* out, int64_t rows,
+                int64_t cols, int dtype, void* stream);
+
+/*
+ * SwiGLU: out = round(g / (1 + exp(-g)) * u) with g = gate, u = up.
+ * Replaces silu_mul_kernel (native/asr/src/decoder.cu:103-109), which writes
+ * into the gate buffer (out == gate is allowed).  Row strides are in
+ * elements, so a packed [rows, 2*cols] gate|up buffer is expressed as
+ * gate = buf, up = buf + cols, gate_stride = up_stride = 2*cols.
+ */
+VL_EXPORT int vl_swiglu(const void* gate, const void* up, void* out, int64_t rows,
+              int64_t cols, int64_t gate_stride, int64_t up_stride,
+              int64_t out_stride, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Rotary embedding                                                          */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Rotate-half RoPE applied in place to q [tokens][n_q_heads][head_dim] and
+ * k [tokens][n_k_heads][head_dim] (row strides in elements; k may be NULL
+ * with n_k_heads == 0).  For every head the first `rotary_dim` dims rotate
+ * in pairs (d, d + rotary_dim/2):
+ *   x1' = x1*cos - x2*sin,  x2' = x2*cos + x1*sin   (fp32, one rounding)
+ * with angle = pos * base^(-2d/rotary_dim) and cos/sin evaluated in fp64 and
+ * rounded to fp32, as the reference's host tables are
+ * (native/asr/src/engine.cu:892-905, native/asr/src/decoder.cu:950-961).
+ * Dims >= rotary_dim are untouched.
+ *
+ * Position of row r:
+ *   positions == NULL:  pos_offset + (seq_len > 0 ? r % seq_len : r)
+ *   positions != NULL:  pos_offset + positions[(row_map ? row_map[r] : r) * positions_stride]
+ * This covers every reference variant: rope_kernel (row % 1500, rotary 32 of
+ * 64), rope_rows_kernel (row % L), rope_full_kernel / rope_at_position_kernel
+ * (seq_len = 1, pos_offset = position), rope_at_position_dev_kernel
+ * (positions_stride = 0), rope_at_position_map_kernel (row_map = active ids)
+ * (engine.cu:217-233; decoder.cu:113-134,307-333,471-498,670-695,789-814).
+ */
+VL_EXPORT int vl_rope_inplace(void* q, void* k, const int32_t* positions,
+                    const int32_t* row_map, int64_t positions_stride,
+                    int64_t pos_offset, int64_t tokens, int64_t seq_len,
+                    int n_q_heads, int n_k_heads, int head_dim, int rotary_dim,
+                    double base, int64_t q_row_stride, int64_t k_row_stride,
+                    int dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Index ops (bit-exact)                                                     */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Token-embedding gather with audio-placeholder substitution.
+ * Output row (b, s), b < batch, s < seq, is out[(b*seq + s)*dim ..]:
+ *   src = row_map ? row_map[b] : b
+ *   id  = ids[src*ids_batch_stride + s]
+ *   id == audio_token_id (>= 0):  audio[src*audio_batch_stride + j*dim ..]
+ *        with j = number of placeholders in ids[src][0..s)
+ *   otherwise:                    table[id*dim ..]
+ * Replaces gather_inputs_kernel, gather_batch_kernel (ids shared by every
+ * chunk: ids_batch_stride = 0), gather_ids_batched_kernel (seq = 1) and
+ * gather_ids_mapped_kernel (row_map = active ids)
+ * (native/asr/src/decoder.cu:60-78, :636-654, :659-667, :460-469).
+ * audio_token_id < 0 disables substitution (audio may then be NULL).
+ * Bad ids (outside [0,vocab)) and placeholders beyond audio_rows give a
+ * zero row and set VL_STATUS_BAD_ID / VL_STATUS_BAD_AUDIO in *status.
+ * dtype only fixes the element size; rows are copied bit for bit.
+ */
+VL_EXPORT int vl_embed_gather(const int64_t* ids, int64_t batch, int64_t seq,
+                    int64_t ids_batch_stride, const int32_t* row_map,
+                    const void* table, int64_t vocab, int64_t dim,
+                    const void* audio, int64_t audio_token_id,
+                    int64_t audio_rows, int64_t audio_batch_stride, void* out,
+                    int dtype, int32_t* status, void* stream);
+
+/*
+ * KV-cache append through a slot mapping.  Caches are
+ * [num_slots][kv_heads*head_dim]; token t's K row (k + t*k_row_stride) and
+ * V row go to slot slot_mapping[t].  slot < 0 skips the token (padding);
+ * slot >= num_slots skips it and sets VL_STATUS_BAD_SLOT.
+ * Replaces append_kv_kernel, append_kv_rows_kernel, append_kv_batched_kernel,
+ * append_kv_batched_dev_kernel and append_kv_mapped_kernel
+ * (native/asr/src/decoder.cu:940-948, :873-882, :857-870, :335-351,
+ * :500-514): their position/chunk-stride addressing is the slot
+ * chunk*(chunk_stride/row) + position.
+ */
+VL_EXPORT int vl_kv_append(const void* k, const void* v, void* k_cache, void* v_cache,
+                 const int64_t* slot_mapping, int64_t tokens, int kv_heads,
+                 int head_dim, int64_t k_row_stride, int64_t v_row_stride,
+                 int64_t num_slots, int dtype, int32_t* status, void* stream);
+
+/*
+ * Decode-step fusion of RoPE and KV append (one launch instead of
+ * rope_at_position_map_kernel + append_kv_mapped_kernel,
+ * native/asr/src/decoder.cu:1710-1718): q is rotated in place; k is rotated,
+ * written back in place AND stored to k_cache[slot]; v is copied to
+ * v_cache[slot].  Row r uses position positions[r] and slot
+ * slot_mapping[r] (slot < 0: q/k still rotate, nothing is cached).
+ */
+VL_EXPORT int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache,
+                      void* v_cache, const int32_t* positions,
+                      const int64_t* slot_mapping, int64_t tokens,
+                      int n_q_heads, int n_k_heads, int head_dim,
+                      int rotary_dim, double base, int64_t num_slots,
+                      int dtype, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* VL_API_H_ */

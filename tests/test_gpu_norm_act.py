@@ -1,0 +1,180 @@
+"""GPU parity: fused residual-add + LayerNorm / RMSNorm, GELU, SwiGLU against
+the CPU oracle (vl_oracle.c), through the C ABI.
+
+Tolerance: normwise relative error <= 1e-5 (fp32), 2e-3 (fp16), 2e-2 (bf16);
+the rounded residual write-back is bit-exact (one fp32 add, one RNE)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import vlasr
+from helpers import TOL, from_np, normwise, to_np, torch_dtype
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = ["f32", "f16", "bf16"]
+NORM_SHAPES = [(1, 1280), (3, 1280), (1500, 1280), (7, 2048), (64, 2048), (5, 7), (2, 1281),
+               (4, 4096), (3, 6000), (2, 64), (9, 520), (1, 8)]
+
+
+def _inputs(rows, cols, dtype, seed, weight_mean=1.0):
+    rng = np.random.default_rng(seed)
+    res = oracle.round_to(rng.normal(0, 1, (rows, cols)), dtype)
+    delta = oracle.round_to(rng.normal(0, 1, (rows, cols)), dtype)
+    gamma = oracle.round_to(rng.normal(weight_mean, 0.02, cols), dtype)
+    beta = oracle.round_to(rng.normal(0, 0.02, cols), dtype)
+    return res, delta, gamma, beta
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", NORM_SHAPES)
+@pytest.mark.parametrize("with_delta", [True, False])
+def test_add_layernorm(dev, dtype, rows, cols, with_delta):
+    res, delta, gamma, beta = _inputs(rows, cols, dtype, seed=rows * 7919 + cols)
+    td = torch_dtype(dtype)
+    r_t, d_t = from_np(res, td, dev), from_np(delta, td, dev)
+    g_t, b_t = from_np(gamma, td, dev), from_np(beta, td, dev)
+    out = vlasr.add_layernorm(r_t, d_t if with_delta else None, g_t, b_t, eps=1e-5)
+    torch.cuda.synchronize()
+    exp_res, exp_out = oracle.add_layernorm(res, delta if with_delta else None, gamma, beta, 1e-5, dtype)
+    np.testing.assert_array_equal(to_np(r_t), exp_res)
+    assert normwise(to_np(out), exp_out) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", NORM_SHAPES)
+@pytest.mark.parametrize("with_delta", [True, False])
+def test_add_rmsnorm(dev, dtype, rows, cols, with_delta):
+    res, delta, w, _ = _inputs(rows, cols, dtype, seed=rows * 104729 + cols)
+    td = torch_dtype(dtype)
+    r_t, d_t, w_t = from_np(res, td, dev), from_np(delta, td, dev), from_np(w, td, dev)
+    out = vlasr.add_rmsnorm(r_t, d_t if with_delta else None, w_t, eps=1e-5)
+    torch.cuda.synchronize()
+    exp_res, exp_out = oracle.add_rmsnorm(res, delta if with_delta else None, w, 1e-5, dtype)
+    np.testing.assert_array_equal(to_np(r_t), exp_res)
+    assert normwise(to_np(out), exp_out) <= TOL[dtype]
+
+
+def test_layernorm_in_place_and_aliasing(dev):
+    """out == residual (reference in-place LN) and out == delta (the layer chain)."""
+    res, delta, gamma, beta = _inputs(33, 1280, "bf16", seed=5)
+    td = torch.bfloat16
+    x = from_np(res, td, dev)
+    vlasr.add_layernorm(x, None, from_np(gamma, td, dev), from_np(beta, td, dev), out=x)
+    _, exp = oracle.add_layernorm(res, None, gamma, beta, 1e-5, "bf16")
+    assert normwise(to_np(x), exp) <= TOL["bf16"]
+    r = from_np(res, td, dev)
+    d = from_np(delta, td, dev)
+    vlasr.add_layernorm(r, d, from_np(gamma, td, dev), from_np(beta, td, dev), out=d)
+    exp_res, exp = oracle.add_layernorm(res, delta, gamma, beta, 1e-5, "bf16")
+    np.testing.assert_array_equal(to_np(r), exp_res)
+    assert normwise(to_np(d), exp) <= TOL["bf16"]
+
+
+def test_layernorm_without_beta_and_degenerate_rows(dev):
+    res = np.zeros((4, 1280), np.float32)
+    res[1] = 1000.0           # constant row: variance 0 (clamped, finite output)
+    res[2, ::2] = 3.0
+    gamma = np.ones(1280, np.float32)
+    r = from_np(res, torch.float32, dev)
+    out = vlasr.add_layernorm(r, None, from_np(gamma, torch.float32, dev), None)
+    o = to_np(out)
+    assert np.isfinite(o).all()
+    _, exp = oracle.add_layernorm(res, None, gamma, None, 1e-5, "f32")
+    np.testing.assert_allclose(o, exp, atol=1e-4)
+
+
+def test_encoder_config_add_layernorm_full_size(dev):
+    """Config 1: [8, 1500, 1280] bf16, x/residual N(0,1), gamma N(1,.02), beta N(0,.02)."""
+    rows, cols = 8 * 1500, 1280
+    res, delta, gamma, beta = _inputs(rows, cols, "bf16", seed=1)
+    td = torch.bfloat16
+    r_t, d_t = from_np(res, td, dev), from_np(delta, td, dev)
+    out = vlasr.add_layernorm(r_t, d_t, from_np(gamma, td, dev), from_np(beta, td, dev))
+    exp_res, exp = oracle.add_layernorm(res, delta, gamma, beta, 1e-5, "bf16")
+    np.testing.assert_array_equal(to_np(r_t), exp_res)
+    err = normwise(to_np(out), exp)
+    assert err <= TOL["bf16"]
+    # identical rounding points: almost every element matches to the last bit
+    assert (to_np(out) == exp).mean() > 0.97
+
+
+def test_decoder_config_add_rmsnorm_full_size(dev):
+    """Config 2: [4, 2048, 2048] bf16."""
+    rows, cols = 4 * 2048, 2048
+    res, delta, w, _ = _inputs(rows, cols, "bf16", seed=2)
+    td = torch.bfloat16
+    r_t, d_t = from_np(res, td, dev), from_np(delta, td, dev)
+    out = vlasr.add_rmsnorm(r_t, d_t, from_np(w, td, dev))
+    exp_res, exp = oracle.add_rmsnorm(res, delta, w, 1e-5, "bf16")
+    np.testing.assert_array_equal(to_np(r_t), exp_res)
+    assert normwise(to_np(out), exp) <= TOL["bf16"]
+    assert (to_np(out) == exp).mean() > 0.97
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", [(1,), (7,), (3, 5), (1500, 1280), (2, 5120), (1, 4104), (4, 8, 520)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_gelu(dev, dtype, shape, with_bias):
+    rng = np.random.default_rng(sum(shape) + 17)
+    x = oracle.round_to(rng.normal(0, 3, shape), dtype)
+    b = oracle.round_to(rng.normal(0, 0.5, shape[-1]), dtype)
+    td = torch_dtype(dtype)
+    out = vlasr.gelu_erf(from_np(x, td, dev), from_np(b, td, dev) if with_bias else None)
+    exp = oracle.gelu(x.reshape(-1, shape[-1]), b if with_bias else None, dtype).reshape(shape)
+    assert normwise(to_np(out), exp) <= TOL[dtype]
+
+
+def test_gelu_in_place_and_full_config(dev):
+    """Config 1 GELU: [8, 1500, 5120] bf16 N(0,1), in place."""
+    rng = np.random.default_rng(11)
+    x = oracle.round_to(rng.normal(0, 1, (8 * 1500, 5120)), "bf16")
+    t = from_np(x, torch.bfloat16, dev)
+    vlasr.gelu_erf(t, out=t)
+    exp = oracle.gelu(x, None, "bf16")
+    got = to_np(t)
+    assert normwise(got, exp) <= TOL["bf16"]
+    assert (got == exp).mean() > 0.999
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (64, 6144), (5, 4104), (2, 520)])
+def test_swiglu(dev, dtype, rows, cols):
+    rng = np.random.default_rng(rows * 31 + cols)
+    g = oracle.round_to(rng.normal(0, 3, (rows, cols)), dtype)
+    u = oracle.round_to(rng.normal(0, 1, (rows, cols)), dtype)
+    td = torch_dtype(dtype)
+    out = vlasr.swiglu(from_np(g, td, dev), from_np(u, td, dev))
+    exp = oracle.swiglu(g, u, dtype)
+    assert normwise(to_np(out), exp) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_swiglu_packed_gate_up_and_in_place(dev, dtype):
+    rng = np.random.default_rng(3)
+    rows, cols = 37, 2048
+    packed = oracle.round_to(rng.normal(0, 2, (rows, 2 * cols)), dtype)
+    td = torch_dtype(dtype)
+    buf = from_np(packed, td, dev)
+    gate, up = buf[:, :cols], buf[:, cols:]
+    out = vlasr.swiglu(gate, up)
+    exp = oracle.swiglu(packed[:, :cols], packed[:, cols:], dtype)
+    assert normwise(to_np(out), exp) <= TOL[dtype]
+    vlasr.swiglu(gate, up, out=gate)  # reference convention: result in the gate buffer
+    assert normwise(to_np(buf[:, :cols]), exp) <= TOL[dtype]
+    np.testing.assert_array_equal(to_np(buf[:, cols:]), packed[:, cols:])
+
+
+def test_swiglu_full_config(dev):
+    """Config 2 SwiGLU: gate, up [4, 2048, 6144] bf16 N(0,1)."""
+    rng = np.random.default_rng(12)
+    shape = (4 * 2048, 6144)
+    g = oracle.round_to(rng.normal(0, 1, shape), "bf16")
+    u = oracle.round_to(rng.normal(0, 1, shape), "bf16")
+    out = vlasr.swiglu(from_np(g, torch.bfloat16, dev), from_np(u, torch.bfloat16, dev))
+    exp = oracle.swiglu(g, u, "bf16")
+    assert normwise(to_np(out), exp) <= TOL["bf16"]

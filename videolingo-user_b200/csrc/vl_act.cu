@@ -1,0 +1,257 @@
+// Exact-erf GELU (optionally bias-fused) and SwiGLU for sm_100a.
+//
+// Reference semantics (VideoLingo-user native/asr/src):
+//   gelu (engine.cu:110-112)          0.5f*x*(1+erff(x*0.70710678118654752440f))
+//   gelu_kernel (engine.cu:194-198)   x = half(gelu(float(x))), in place
+//   add_bias_kernel (engine.cu:200-205) x = half(float(x) + float(b[col]))
+//   silu_mul_kernel (decoder.cu:103-109) g = half(g / (1 + __expf(-g)) * u)
+// Both are pure streams: 16-byte vector loads, several vectors in flight per
+// thread, grid sized to a whole number of waves over the SMs.
+#include "vl_common.cuh"
+#include "vl_kernels.h"
+
+namespace vl {
+namespace {
+
+constexpr int kActThreads = 256;
+constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return g / (1.0f + __expf(-g)) * u;
+}
+
+// Contiguous GELU without bias: flat grid-stride over 16-byte vectors.
+template <typename T>
+__global__ void __launch_bounds__(kActThreads)
+    gelu_flat_kernel(const T* in, T* out, int64_t nvec) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  const uint4* src = reinterpret_cast<const uint4*>(in);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kActThreads * kUnroll;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kActThreads * kUnroll + threadIdx.x;
+       base < nvec; base += step) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kActThreads;
+      if (i < nvec) v[u] = ld_stream(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kActThreads;
+      if (i < nvec) {
+        float f[E];
+        S::unpack(v[u], f);
+#pragma unroll
+        for (int e = 0; e < E; ++e) f[e] = gelu_erf(f[e]);
+        st_stream(dst + i, S::pack(f));
+      }
+    }
+  }
+}
+
+// Row-structured GELU with bias: blockIdx.y strides rows, threads cover the
+// row's vectors.  t = round(x + b) is formed before GELU, as the reference
+// stores the biased activation before gelu_kernel reads it.
+template <typename T>
+__global__ void __launch_bounds__(kActThreads)
+    gelu_bias_kernel(const T* in, const T* __restrict__ bias, T* out, int64_t rows,
+                     int vec_per_row) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  const int v = blockIdx.x * kActThreads + threadIdx.x;
+  if (v >= vec_per_row) return;
+  float b[E];
+  S::unpack(__ldg(reinterpret_cast<const uint4*>(bias) + v), b);
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int64_t i = r * vec_per_row + v;
+    float f[E];
+    S::unpack(ld_stream(reinterpret_cast<const uint4*>(in) + i), f);
+#pragma unroll
+    for (int e = 0; e < E; ++e) f[e] = gelu_erf(S::round_trip(f[e] + b[e]));
+    st_stream(reinterpret_cast<uint4*>(out) + i, S::pack(f));
+  }
+}
+
+// Any shape / alignment.
+template <typename T>
+__global__ void gelu_scalar_kernel(const T* in, const T* bias, T* out, int64_t rows,
+                                   int64_t cols) {
+  using S = Storage<T>;
+  const int64_t n = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float x = S::to_float(in[i]);
+    if (bias) x = S::round_trip(x + S::to_float(bias[i % cols]));
+    out[i] = S::from_float(gelu_erf(x));
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kActThreads)
+    swiglu_flat_kernel(const T* gate, const T* up, T* out, int64_t nvec) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  const uint4* g4 = reinterpret_cast<const uint4*>(gate);
+  const uint4* u4 = reinterpret_cast<const uint4*>(up);
+  uint4* o4 = reinterpret_cast<uint4*>(out);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kActThreads * kUnroll;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kActThreads * kUnroll + threadIdx.x;
+       base < nvec; base += step) {
+    uint4 gv[kUnroll], uv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kActThreads;
+      if (i < nvec) {
+        gv[u] = ld_stream(g4 + i);
+        uv[u] = ld_stream(u4 + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kActThreads;
+      if (i < nvec) {
+        float g[E], x[E];
+        S::unpack(gv[u], g);
+        S::unpack(uv[u], x);
+#pragma unroll
+        for (int e = 0; e < E; ++e) g[e] = silu_mul(g[e], x[e]);
+        st_stream(o4 + i, S::pack(g));
+      }
+    }
+  }
+}
+
+// Strided rows (packed gate|up layouts): blockIdx.y strides rows.
+template <typename T>
+__global__ void __launch_bounds__(kActThreads)
+    swiglu_rows_kernel(const T* gate, const T* up, T* out, int64_t rows, int vec_per_row,
+                       int64_t gs, int64_t us, int64_t os) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  const int v = blockIdx.x * kActThreads + threadIdx.x;
+  if (v >= vec_per_row) return;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    float g[E], x[E];
+    S::unpack(ld_stream(reinterpret_cast<const uint4*>(gate + r * gs) + v), g);
+    S::unpack(ld_stream(reinterpret_cast<const uint4*>(up + r * us) + v), x);
+#pragma unroll
+    for (int e = 0; e < E; ++e) g[e] = silu_mul(g[e], x[e]);
+    st_stream(reinterpret_cast<uint4*>(out + r * os) + v, S::pack(g));
+  }
+}
+
+template <typename T>
+__global__ void swiglu_scalar_kernel(const T* gate, const T* up, T* out, int64_t rows,
+                                     int64_t cols, int64_t gs, int64_t us, int64_t os) {
+  using S = Storage<T>;
+  const int64_t n = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    out[r * os + c] = S::from_float(silu_mul(S::to_float(gate[r * gs + c]),
+                                             S::to_float(up[r * us + c])));
+  }
+}
+
+unsigned flat_blocks(int64_t nvec) {
+  const int64_t per_block = static_cast<int64_t>(kActThreads) * kUnroll;
+  const int64_t need = (nvec + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 x 256 threads resident per SM
+  return static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+dim3 row_grid(int vec_per_row, int64_t rows) {
+  const unsigned gx = static_cast<unsigned>((vec_per_row + kActThreads - 1) / kActThreads);
+  const int64_t want = (static_cast<int64_t>(sm_count()) * 8 + gx - 1) / gx;
+  int64_t gy = rows < want ? rows : want;
+  if (gy > 65535) gy = 65535;
+  if (gy < 1) gy = 1;
+  return dim3(gx, static_cast<unsigned>(gy), 1);
+}
+
+template <typename T>
+cudaError_t gelu_typed(const void* in, const void* bias, void* out, int64_t rows, int64_t cols,
+                       cudaStream_t stream) {
+  constexpr int E = Storage<T>::kVec;
+  const T* x = static_cast<const T*>(in);
+  T* y = static_cast<T*>(out);
+  const bool vec_ok = aligned16(in) && aligned16(out) && (bias == nullptr || aligned16(bias));
+  if (bias == nullptr && vec_ok && ((rows * cols) % E == 0)) {
+    const int64_t nvec = rows * cols / E;
+    gelu_flat_kernel<T><<<flat_blocks(nvec), kActThreads, 0, stream>>>(x, y, nvec);
+  } else if (bias != nullptr && vec_ok && cols % E == 0 && cols / E < (1 << 30)) {
+    const int vpr = static_cast<int>(cols / E);
+    gelu_bias_kernel<T><<<row_grid(vpr, rows), kActThreads, 0, stream>>>(
+        x, static_cast<const T*>(bias), y, rows, vpr);
+  } else {
+    const int64_t n = rows * cols;
+    int64_t blocks = (n + kActThreads - 1) / kActThreads;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    if (blocks > cap) blocks = cap;
+    gelu_scalar_kernel<T><<<static_cast<unsigned>(blocks), kActThreads, 0, stream>>>(
+        x, static_cast<const T*>(bias), y, rows, cols);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t swiglu_typed(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+                         int64_t gs, int64_t us, int64_t os, cudaStream_t stream) {
+  constexpr int E = Storage<T>::kVec;
+  const T* g = static_cast<const T*>(gate);
+  const T* u = static_cast<const T*>(up);
+  T* o = static_cast<T*>(out);
+  const bool vec_ok = aligned16(gate) && aligned16(up) && aligned16(out) && cols % E == 0 &&
+                      gs % E == 0 && us % E == 0 && os % E == 0;
+  if (vec_ok && gs == cols && us == cols && os == cols) {
+    const int64_t nvec = rows * cols / E;
+    swiglu_flat_kernel<T><<<flat_blocks(nvec), kActThreads, 0, stream>>>(g, u, o, nvec);
+  } else if (vec_ok && cols / E < (1 << 30)) {
+    const int vpr = static_cast<int>(cols / E);
+    swiglu_rows_kernel<T><<<row_grid(vpr, rows), kActThreads, 0, stream>>>(g, u, o, rows, vpr, gs,
+                                                                          us, os);
+  } else {
+    const int64_t n = rows * cols;
+    int64_t blocks = (n + kActThreads - 1) / kActThreads;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    if (blocks > cap) blocks = cap;
+    swiglu_scalar_kernel<T><<<static_cast<unsigned>(blocks), kActThreads, 0, stream>>>(
+        g, u, o, rows, cols, gs, us, os);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gelu(const void* in, const void* bias, void* out, int64_t rows, int64_t cols,
+                        int dtype, cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtypeF32: return gelu_typed<float>(in, bias, out, rows, cols, stream);
+    case kDtypeF16: return gelu_typed<__half>(in, bias, out, rows, cols, stream);
+    default: return gelu_typed<__nv_bfloat16>(in, bias, out, rows, cols, stream);
+  }
+}
+
+cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+                          int64_t gate_stride, int64_t up_stride, int64_t out_stride, int dtype,
+                          cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtypeF32:
+      return swiglu_typed<float>(gate, up, out, rows, cols, gate_stride, up_stride, out_stride, stream);
+    case kDtypeF16:
+      return swiglu_typed<__half>(gate, up, out, rows, cols, gate_stride, up_stride, out_stride, stream);
+    default:
+      return swiglu_typed<__nv_bfloat16>(gate, up, out, rows, cols, gate_stride, up_stride,
+                                         out_stride, stream);
+  }
+}
+
+}  // namespace vl

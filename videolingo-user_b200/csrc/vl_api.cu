@@ -1,0 +1,333 @@
+// C ABI of libvlasr.so (declared in include/vl_api.h).
+//
+// Every entry point validates its arguments on the host before touching
+// CUDA, maps failures onto the reference CLI's status taxonomy
+// (native/asr/src/main_m0.cu:696-703: 2 = invalid input, 1 = execution
+// failure) and records a message for vl_last_error().  No exception crosses
+// the boundary, nothing is allocated and nothing synchronises.
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "vl_common.cuh"
+#include "vl_kernels.h"
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_error[0] = '\0';
+  return VL_OK;
+}
+
+int exec_status(cudaError_t err, const char* op) {
+  if (err == cudaSuccess) return ok();
+  return fail(VL_ERR_EXEC, "%s: CUDA error %d (%s)", op, static_cast<int>(err),
+              cudaGetErrorString(err));
+}
+
+bool valid_dtype(int dtype) {
+  return dtype == VL_F32 || dtype == VL_F16 || dtype == VL_BF16;
+}
+
+int64_t dtype_size(int dtype) { return dtype == VL_F32 ? 4 : 2; }
+
+bool overlaps(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + static_cast<uintptr_t>(b_bytes) && y < x + static_cast<uintptr_t>(a_bytes);
+}
+
+constexpr int64_t kMaxRows = int64_t(1) << 40;
+constexpr int64_t kMaxCols = int64_t(1) << 30;
+constexpr int64_t kMaxMelChunks = int64_t(1) << 20;
+
+}  // namespace
+
+namespace vl {
+
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+    v = 148;
+  cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+}  // namespace vl
+
+extern "C" {
+
+int vl_version(void) { return 100; }
+
+const char* vl_last_error(void) { return g_error; }
+
+int vl_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+size_t vl_logmel_workspace_bytes(int64_t chunks) {
+  if (chunks <= 0 || chunks > kMaxMelChunks) return 0;
+  return vl::logmel_workspace_bytes(chunks);
+}
+
+int vl_logmel(const float* pcm, int64_t chunks, float* out, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  if (pcm == nullptr || out == nullptr || workspace == nullptr)
+    return fail(VL_ERR_INVALID, "vl_logmel: null pointer (pcm=%p out=%p workspace=%p)", pcm, out,
+                workspace);
+  if (chunks <= 0 || chunks > kMaxMelChunks)
+    return fail(VL_ERR_INVALID, "vl_logmel: chunks must be in [1, %lld], got %lld",
+                static_cast<long long>(kMaxMelChunks), static_cast<long long>(chunks));
+  if (!vl::aligned16(pcm) || !vl::aligned16(out) || !vl::aligned16(workspace))
+    return fail(VL_ERR_INVALID, "vl_logmel: pcm, out and workspace must be 16-byte aligned");
+  const size_t need = vl::logmel_workspace_bytes(chunks);
+  if (workspace_bytes < need)
+    return fail(VL_ERR_INVALID, "vl_logmel: workspace holds %zu bytes, %zu needed", workspace_bytes,
+                need);
+  const int64_t in_bytes = chunks * VL_MEL_CHUNK_SAMPLES * 4;
+  const int64_t out_bytes = chunks * VL_MEL_BINS * VL_MEL_FRAMES * 4;
+  if (overlaps(pcm, in_bytes, out, out_bytes) || overlaps(workspace, static_cast<int64_t>(need), out, out_bytes) ||
+      overlaps(workspace, static_cast<int64_t>(need), pcm, in_bytes))
+    return fail(VL_ERR_INVALID, "vl_logmel: pcm, out and workspace must not overlap");
+  return exec_status(vl::launch_logmel(pcm, chunks, out, static_cast<float*>(workspace),
+                                       static_cast<cudaStream_t>(stream)),
+                     "vl_logmel");
+}
+
+static int check_norm(const char* op, void* residual, const void* delta, const void* weight,
+                      void* out, int64_t rows, int64_t cols, float eps, int dtype) {
+  if (residual == nullptr || weight == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "%s: null pointer (residual=%p weight=%p out=%p)", op, residual,
+                weight, out);
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "%s: unsupported dtype %d", op, dtype);
+  if (rows < 0 || rows > kMaxRows || cols <= 0 || cols > kMaxCols)
+    return fail(VL_ERR_INVALID, "%s: bad shape rows=%lld cols=%lld", op,
+                static_cast<long long>(rows), static_cast<long long>(cols));
+  if (!(eps >= 0.f) || !std::isfinite(eps))
+    return fail(VL_ERR_INVALID, "%s: eps must be finite and >= 0", op);
+  if (delta != nullptr) {
+    const int64_t bytes = rows * cols * dtype_size(dtype);
+    if (overlaps(out, bytes, residual, bytes))
+      return fail(VL_ERR_INVALID, "%s: out must not alias residual when delta is given", op);
+    if (delta != out && overlaps(delta, bytes, residual, bytes))
+      return fail(VL_ERR_INVALID, "%s: delta must not alias residual", op);
+  }
+  return VL_OK;
+}
+
+int vl_add_layernorm(void* residual, const void* delta, const void* gamma, const void* beta,
+                     void* out, int64_t rows, int64_t cols, float eps, int dtype, void* stream) {
+  const int st = check_norm("vl_add_layernorm", residual, delta, gamma, out, rows, cols, eps, dtype);
+  if (st != VL_OK) return st;
+  return exec_status(vl::launch_add_norm(residual, delta, gamma, beta, out, rows, cols, eps, false,
+                                         dtype, static_cast<cudaStream_t>(stream)),
+                     "vl_add_layernorm");
+}
+
+int vl_add_rmsnorm(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
+                   int64_t cols, float eps, int dtype, void* stream) {
+  const int st = check_norm("vl_add_rmsnorm", residual, delta, weight, out, rows, cols, eps, dtype);
+  if (st != VL_OK) return st;
+  return exec_status(vl::launch_add_norm(residual, delta, weight, nullptr, out, rows, cols, eps,
+                                         true, dtype, static_cast<cudaStream_t>(stream)),
+                     "vl_add_rmsnorm");
+}
+
+int vl_gelu_erf(const void* in, const void* bias, void* out, int64_t rows, int64_t cols, int dtype,
+                void* stream) {
+  if (in == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_gelu_erf: null pointer (in=%p out=%p)", in, out);
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "vl_gelu_erf: unsupported dtype %d", dtype);
+  if (rows < 0 || rows > kMaxRows || cols < 0 || cols > kMaxCols)
+    return fail(VL_ERR_INVALID, "vl_gelu_erf: bad shape rows=%lld cols=%lld",
+                static_cast<long long>(rows), static_cast<long long>(cols));
+  if (in != out) {
+    const int64_t bytes = rows * cols * dtype_size(dtype);
+    if (overlaps(in, bytes, out, bytes))
+      return fail(VL_ERR_INVALID, "vl_gelu_erf: in and out overlap without being equal");
+  }
+  return exec_status(vl::launch_gelu(in, bias, out, rows, cols, dtype, static_cast<cudaStream_t>(stream)),
+                     "vl_gelu_erf");
+}
+
+int vl_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+              int64_t gate_stride, int64_t up_stride, int64_t out_stride, int dtype, void* stream) {
+  if (gate == nullptr || up == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_swiglu: null pointer (gate=%p up=%p out=%p)", gate, up, out);
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "vl_swiglu: unsupported dtype %d", dtype);
+  if (rows < 0 || rows > kMaxRows || cols < 0 || cols > kMaxCols)
+    return fail(VL_ERR_INVALID, "vl_swiglu: bad shape rows=%lld cols=%lld",
+                static_cast<long long>(rows), static_cast<long long>(cols));
+  if (gate_stride < cols || up_stride < cols || out_stride < cols)
+    return fail(VL_ERR_INVALID, "vl_swiglu: row strides must be >= cols");
+  if (out != gate && out != up && rows > 0 && cols > 0) {
+    const int64_t es = dtype_size(dtype);
+    const int64_t ob = ((rows - 1) * out_stride + cols) * es;
+    if (overlaps(out, ob, gate, ((rows - 1) * gate_stride + cols) * es) ||
+        overlaps(out, ob, up, ((rows - 1) * up_stride + cols) * es))
+      return fail(VL_ERR_INVALID, "vl_swiglu: out overlaps an input without being equal to it");
+  }
+  return exec_status(vl::launch_swiglu(gate, up, out, rows, cols, gate_stride, up_stride, out_stride,
+                                       dtype, static_cast<cudaStream_t>(stream)),
+                     "vl_swiglu");
+}
+
+static int check_rope(const char* op, const void* q, const void* k, int64_t tokens, int n_q_heads,
+                      int n_k_heads, int head_dim, int rotary_dim, double base,
+                      int64_t q_row_stride, int64_t k_row_stride, int dtype) {
+  if (q == nullptr && n_q_heads > 0) return fail(VL_ERR_INVALID, "%s: q is null", op);
+  if ((k == nullptr) != (n_k_heads == 0))
+    return fail(VL_ERR_INVALID, "%s: k must be null exactly when n_k_heads == 0", op);
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "%s: unsupported dtype %d", op, dtype);
+  if (tokens < 0 || tokens > kMaxRows || n_q_heads < 0 || n_k_heads < 0 ||
+      n_q_heads + n_k_heads == 0)
+    return fail(VL_ERR_INVALID, "%s: bad shape tokens=%lld heads=%d/%d", op,
+                static_cast<long long>(tokens), n_q_heads, n_k_heads);
+  if (head_dim <= 0 || rotary_dim <= 0 || rotary_dim % 2 != 0 || rotary_dim > head_dim ||
+      rotary_dim > 256)
+    return fail(VL_ERR_INVALID,
+                "%s: rotary_dim must be even, in (0, min(head_dim, 256)] (head_dim=%d rotary_dim=%d)",
+                op, head_dim, rotary_dim);
+  if (!(base > 0.0) || !std::isfinite(base))
+    return fail(VL_ERR_INVALID, "%s: base must be finite and > 0", op);
+  if (q_row_stride < static_cast<int64_t>(n_q_heads) * head_dim ||
+      (n_k_heads > 0 && k_row_stride < static_cast<int64_t>(n_k_heads) * head_dim))
+    return fail(VL_ERR_INVALID, "%s: row strides must cover heads * head_dim", op);
+  return VL_OK;
+}
+
+int vl_rope_inplace(void* q, void* k, const int32_t* positions, const int32_t* row_map,
+                    int64_t positions_stride, int64_t pos_offset, int64_t tokens, int64_t seq_len,
+                    int n_q_heads, int n_k_heads, int head_dim, int rotary_dim, double base,
+                    int64_t q_row_stride, int64_t k_row_stride, int dtype, void* stream) {
+  const int st = check_rope("vl_rope_inplace", q, k, tokens, n_q_heads, n_k_heads, head_dim,
+                            rotary_dim, base, q_row_stride, k_row_stride, dtype);
+  if (st != VL_OK) return st;
+  if (seq_len < 0 || positions_stride < 0)
+    return fail(VL_ERR_INVALID, "vl_rope_inplace: seq_len and positions_stride must be >= 0");
+  if (row_map != nullptr && positions == nullptr)
+    return fail(VL_ERR_INVALID, "vl_rope_inplace: row_map requires positions");
+  if (n_q_heads == 0 && q == nullptr) q = k;  // only K rotates; q is never dereferenced
+  vl::RopeArgs a{};
+  a.q = q;
+  a.k = k;
+  a.positions = positions;
+  a.row_map = row_map;
+  a.positions_stride = positions_stride;
+  a.pos_offset = pos_offset;
+  a.tokens = tokens;
+  a.seq_len = seq_len;
+  a.n_q_heads = n_q_heads;
+  a.n_k_heads = n_k_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.base = base;
+  a.q_row_stride = q_row_stride;
+  a.k_row_stride = k_row_stride;
+  return exec_status(vl::launch_rope(a, dtype, static_cast<cudaStream_t>(stream)), "vl_rope_inplace");
+}
+
+int vl_embed_gather(const int64_t* ids, int64_t batch, int64_t seq, int64_t ids_batch_stride,
+                    const int32_t* row_map, const void* table, int64_t vocab, int64_t dim,
+                    const void* audio, int64_t audio_token_id, int64_t audio_rows,
+                    int64_t audio_batch_stride, void* out, int dtype, int32_t* status,
+                    void* stream) {
+  if (ids == nullptr || table == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_embed_gather: null pointer (ids=%p table=%p out=%p)", ids,
+                table, out);
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "vl_embed_gather: unsupported dtype %d", dtype);
+  if (batch < 0 || seq < 0 || batch * seq > kMaxRows || vocab <= 0 || dim <= 0 || dim > kMaxCols ||
+      ids_batch_stride < 0)
+    return fail(VL_ERR_INVALID, "vl_embed_gather: bad shape batch=%lld seq=%lld vocab=%lld dim=%lld",
+                static_cast<long long>(batch), static_cast<long long>(seq),
+                static_cast<long long>(vocab), static_cast<long long>(dim));
+  if (audio_token_id >= 0 && (audio == nullptr || audio_rows < 0 || audio_batch_stride < 0))
+    return fail(VL_ERR_INVALID,
+                "vl_embed_gather: audio substitution needs audio rows (audio=%p rows=%lld)", audio,
+                static_cast<long long>(audio_rows));
+  const int64_t es = dtype_size(dtype);
+  return exec_status(
+      vl::launch_embed_gather(ids, batch, seq, ids_batch_stride, row_map, table, vocab, dim * es,
+                              audio, audio_token_id, audio_rows, audio_batch_stride * es, out,
+                              status, static_cast<cudaStream_t>(stream)),
+      "vl_embed_gather");
+}
+
+int vl_kv_append(const void* k, const void* v, void* k_cache, void* v_cache,
+                 const int64_t* slot_mapping, int64_t tokens, int kv_heads, int head_dim,
+                 int64_t k_row_stride, int64_t v_row_stride, int64_t num_slots, int dtype,
+                 int32_t* status, void* stream) {
+  if (k == nullptr || v == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      slot_mapping == nullptr)
+    return fail(VL_ERR_INVALID, "vl_kv_append: null pointer");
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "vl_kv_append: unsupported dtype %d", dtype);
+  const int64_t row = static_cast<int64_t>(kv_heads) * head_dim;
+  if (tokens < 0 || tokens > kMaxRows || kv_heads <= 0 || head_dim <= 0 || num_slots < 0 ||
+      k_row_stride < row || v_row_stride < row)
+    return fail(VL_ERR_INVALID, "vl_kv_append: bad shape tokens=%lld kv_heads=%d head_dim=%d",
+                static_cast<long long>(tokens), kv_heads, head_dim);
+  const int64_t es = dtype_size(dtype);
+  return exec_status(vl::launch_kv_append(k, v, k_cache, v_cache, slot_mapping, tokens, row * es,
+                                          k_row_stride * es, v_row_stride * es, num_slots, status,
+                                          static_cast<cudaStream_t>(stream)),
+                     "vl_kv_append");
+}
+
+int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache, void* v_cache,
+                      const int32_t* positions, const int64_t* slot_mapping, int64_t tokens,
+                      int n_q_heads, int n_k_heads, int head_dim, int rotary_dim, double base,
+                      int64_t num_slots, int dtype, int32_t* status, void* stream) {
+  const int64_t qs = static_cast<int64_t>(n_q_heads) * head_dim;
+  const int64_t ks = static_cast<int64_t>(n_k_heads) * head_dim;
+  const int st = check_rope("vl_rope_kv_append", q, k, tokens, n_q_heads, n_k_heads, head_dim,
+                            rotary_dim, base, qs, ks, dtype);
+  if (st != VL_OK) return st;
+  if (k == nullptr || v == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      positions == nullptr || slot_mapping == nullptr)
+    return fail(VL_ERR_INVALID, "vl_rope_kv_append: null pointer");
+  if (num_slots < 0) return fail(VL_ERR_INVALID, "vl_rope_kv_append: num_slots must be >= 0");
+  if (n_q_heads == 0 && q == nullptr) q = k;
+  vl::RopeArgs a{};
+  a.q = q;
+  a.k = k;
+  a.positions = positions;
+  a.positions_stride = 1;
+  a.tokens = tokens;
+  a.n_q_heads = n_q_heads;
+  a.n_k_heads = n_k_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.base = base;
+  a.q_row_stride = qs;
+  a.k_row_stride = ks;
+  a.v = v;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.slot_mapping = slot_mapping;
+  a.num_slots = num_slots;
+  a.status = status;
+  return exec_status(vl::launch_rope(a, dtype, static_cast<cudaStream_t>(stream)),
+                     "vl_rope_kv_append");
+}
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// Internal launcher interface between the C ABI (vl_api.cu) and the kernel
+// translation units.  Arguments arrive already validated; every launcher only
+// enqueues work on `stream` and returns the launch status.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace vl {
+
+cudaError_t launch_add_norm(void* residual, const void* delta, const void* gamma,
+                            const void* beta, void* out, int64_t rows, int64_t cols, float eps,
+                            bool rms, int dtype, cudaStream_t stream);
+
+cudaError_t launch_gelu(const void* in, const void* bias, void* out, int64_t rows, int64_t cols,
+                        int dtype, cudaStream_t stream);
+
+cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+                          int64_t gate_stride, int64_t up_stride, int64_t out_stride, int dtype,
+                          cudaStream_t stream);
+
+struct RopeArgs {
+  void* q;
+  void* k;
+  const int32_t* positions;
+  const int32_t* row_map;
+  int64_t positions_stride;
+  int64_t pos_offset;
+  int64_t tokens;
+  int64_t seq_len;
+  int n_q_heads;
+  int n_k_heads;
+  int head_dim;
+  int rotary_dim;
+  double base;
+  int64_t q_row_stride;
+  int64_t k_row_stride;
+  // Fused KV append (vl_rope_kv_append); v == nullptr disables it.
+  const void* v;
+  void* k_cache;
+  void* v_cache;
+  const int64_t* slot_mapping;
+  int64_t num_slots;
+  int32_t* status;
+};
+cudaError_t launch_rope(const RopeArgs& args, int dtype, cudaStream_t stream);
+
+cudaError_t launch_embed_gather(const int64_t* ids, int64_t batch, int64_t seq,
+                                int64_t ids_batch_stride, const int32_t* row_map,
+                                const void* table, int64_t vocab, int64_t row_bytes,
+                                const void* audio, int64_t audio_token_id, int64_t audio_rows,
+                                int64_t audio_batch_stride_bytes, void* out, int32_t* status,
+                                cudaStream_t stream);
+
+cudaError_t launch_kv_append(const void* k, const void* v, void* k_cache, void* v_cache,
+                             const int64_t* slot_mapping, int64_t tokens, int64_t row_bytes,
+                             int64_t k_row_stride_bytes, int64_t v_row_stride_bytes,
+                             int64_t num_slots, int32_t* status, cudaStream_t stream);
+
+size_t logmel_workspace_bytes(int64_t chunks);
+cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
+                          cudaStream_t stream);
+
+}  // namespace vl

@@ -1,0 +1,293 @@
+// Whisper log-mel frontend for sm_100a.
+//
+// Reference: compute_mel_batched (VideoLingo-user
+// native/asr/src/mel_frontend.cu:209-291) runs five kernels per call:
+// a 400-tap direct DFT per (bin, frame) (stft_power_kernel :164-184), a dense
+// 201-term filterbank product (mel_matmul_kernel :187-201), log10 + per-bin
+// max, per-chunk max and the normalise pass (:108-153), with the power and
+// mel spectra making full HBM round trips in between.
+//
+// Here the whole per-frame pipeline is one kernel over tiles of 24 frames:
+//   samples (reflect-padded) -> shared memory
+//   two real frames packed as one complex 400-point FFT (x_a + i*x_b),
+//     400 = 20 x 20: stage 1 = 20 DFT-20s over stride-20 samples + W400
+//     twiddles, stage 2 = 20 DFT-20s (each DFT-20 = 4 x 5 in registers)
+//   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry
+//   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense)
+//   log10(max(., 1e-10)) -> out, tile max -> workspace
+// and a second, light kernel folds the tile maxima of each chunk and applies
+// max(x, max-8) then (x+4)/4 in place.  Chunks are processed in batches whose
+// log-mel (1.5 MB per chunk) stays resident in the 126 MB L2 between the two
+// kernels, so HBM sees the PCM once and the features once.
+#include <atomic>
+
+#include "vl_common.cuh"
+#include "vl_kernels.h"
+#include "mel_tables.inc"
+
+namespace vl {
+namespace {
+
+constexpr int kChunkSamples = 480000;
+constexpr int kHop = 160;
+constexpr int kPad = 200;
+constexpr int kFrames = 3000;              // frames kept (the 3001st is dropped)
+constexpr int kTileFrames = 24;            // frames per tile (divides 3000)
+constexpr int kPairs = kTileFrames / 2;    // complex FFTs per tile
+constexpr int kTilesPerChunk = kFrames / kTileFrames;  // 125
+constexpr int kTileSamples = kHop * (kTileFrames - 1) + 400;  // 4080
+constexpr int kBins = 201;
+constexpr int kMel = 128;
+constexpr int kThreads = 256;
+constexpr int kTRow = 21;                  // padded row (complex) of the stage-1 transpose
+constexpr int kNormSlices = 16;            // normalise blocks per chunk
+constexpr int kBatchChunks = 32;           // chunks per L2-resident batch
+
+struct MelSmem {
+  float samples[kTileSamples];
+  float window[400];
+  float2 tw[400];
+  float2 z[kPairs][400];                   // packed spectra Z[p][k]
+  union {
+    float2 t[kPairs][20][kTRow];           // stage-1 output, transposed
+    float p[kTileFrames][kBins];           // power spectra
+  } u;
+  float melw[VL_MEL_NNZ];
+  int mel_off[kMel + 1];
+  int mel_lo[kMel];
+  float red[kThreads / 32];
+};
+
+struct cpx {
+  float re, im;
+};
+__device__ __forceinline__ cpx cadd(cpx a, cpx b) { return {a.re + b.re, a.im + b.im}; }
+__device__ __forceinline__ cpx csub(cpx a, cpx b) { return {a.re - b.re, a.im - b.im}; }
+// a * conj(w) with w = (cos, sin): multiplies by exp(-i*theta).
+__device__ __forceinline__ cpx cmul_conj(cpx a, float c, float s) {
+  return {a.re * c + a.im * s, a.im * c - a.re * s};
+}
+
+// In-place forward DFT of 20 complex points: X[k] = sum_n x[n] exp(-2 pi i k n / 20).
+// 20 = 4 x 5: n = 5a + b, k = c + 4d.  DFT-4 over a, twiddle W20^(b c),
+// DFT-5 over b.
+__device__ __forceinline__ void dft20(cpx (&x)[20]) {
+  cpx u[5][4];
+#pragma unroll
+  for (int b = 0; b < 5; ++b) {
+    const cpx x0 = x[b], x1 = x[5 + b], x2 = x[10 + b], x3 = x[15 + b];
+    const cpx t0 = cadd(x0, x2), t1 = csub(x0, x2), t2 = cadd(x1, x3), t3 = csub(x1, x3);
+    u[b][0] = cadd(t0, t2);
+    u[b][2] = csub(t0, t2);
+    u[b][1] = {t1.re + t3.im, t1.im - t3.re};  // t1 - i t3
+    u[b][3] = {t1.re - t3.im, t1.im + t3.re};  // t1 + i t3
+  }
+#pragma unroll
+  for (int b = 1; b < 5; ++b)
+#pragma unroll
+    for (int c = 1; c < 4; ++c) {
+      const int j = b * c;
+      u[b][c] = cmul_conj(u[b][c], mel::w20_cos(j), mel::w20_sin(j));
+    }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const cpx x0 = u[0][c], x1 = u[1][c], x2 = u[2][c], x3 = u[3][c], x4 = u[4][c];
+    const cpx a1 = cadd(x1, x4), a2 = cadd(x2, x3), b1 = csub(x1, x4), b2 = csub(x2, x3);
+    const cpx m1 = {x0.re + mel::kC1 * a1.re + mel::kC2 * a2.re,
+                    x0.im + mel::kC1 * a1.im + mel::kC2 * a2.im};
+    const cpx m2 = {x0.re + mel::kC2 * a1.re + mel::kC1 * a2.re,
+                    x0.im + mel::kC2 * a1.im + mel::kC1 * a2.im};
+    const cpx n1 = {mel::kS1 * b1.re + mel::kS2 * b2.re, mel::kS1 * b1.im + mel::kS2 * b2.im};
+    const cpx n2 = {mel::kS2 * b1.re - mel::kS1 * b2.re, mel::kS2 * b1.im - mel::kS1 * b2.im};
+    x[c] = {x0.re + a1.re + a2.re, x0.im + a1.im + a2.im};
+    x[c + 4] = {m1.re + n1.im, m1.im - n1.re};    // m1 - i n1
+    x[c + 16] = {m1.re - n1.im, m1.im + n1.re};   // m1 + i n1
+    x[c + 8] = {m2.re + n2.im, m2.im - n2.re};    // m2 - i n2
+    x[c + 12] = {m2.re - n2.im, m2.im + n2.re};   // m2 + i n2
+  }
+}
+
+__device__ __forceinline__ int reflect(int j) {
+  if (j < 0) return -j;
+  if (j >= kChunkSamples) return 2 * kChunkSamples - 2 - j;
+  return j;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    mel_tile_kernel(const float* __restrict__ pcm, float* __restrict__ out,
+                    float* __restrict__ tile_max, int chunk0) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  MelSmem& sm = *reinterpret_cast<MelSmem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int tile = blockIdx.x;
+  const int64_t chunk = chunk0 + blockIdx.y;
+  const int f0 = tile * kTileFrames;
+  const float* src = pcm + chunk * kChunkSamples;
+  const int j0 = f0 * kHop - kPad;
+
+  // ---- stage 0: samples, window, twiddles and filterbank into shared memory
+  if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + j0);
+    float4* d4 = reinterpret_cast<float4*>(sm.samples);
+    for (int i = tid; i < kTileSamples / 4; i += kThreads) d4[i] = __ldcs(s4 + i);
+  } else {
+    for (int i = tid; i < kTileSamples; i += kThreads) sm.samples[i] = src[reflect(j0 + i)];
+  }
+  for (int i = tid; i < 400; i += kThreads) {
+    sm.window[i] = mel::kWindow[i];
+    sm.tw[i] = mel::kTwiddle400[i];
+  }
+  for (int i = tid; i < VL_MEL_NNZ; i += kThreads) sm.melw[i] = mel::kMelWeights[i];
+  for (int i = tid; i <= kMel; i += kThreads) sm.mel_off[i] = mel::kMelOffset[i];
+  for (int i = tid; i < kMel; i += kThreads) sm.mel_lo[i] = mel::kMelLo[i];
+  __syncthreads();
+
+  // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
+  if (tid < kPairs * 20) {
+    const int p = tid / 20, n2 = tid % 20;
+    const float* sa = sm.samples + 2 * p * kHop;
+    const float* sb = sa + kHop;
+    cpx x[20];
+#pragma unroll
+    for (int n1 = 0; n1 < 20; ++n1) {
+      const int n = 20 * n1 + n2;
+      const float w = sm.window[n];
+      x[n1] = {sa[n] * w, sb[n] * w};
+    }
+    dft20(x);
+#pragma unroll
+    for (int k1 = 0; k1 < 20; ++k1) {
+      const float2 w = sm.tw[k1 * n2];
+      const cpx y = cmul_conj(x[k1], w.x, w.y);
+      sm.u.t[p][k1][n2] = make_float2(y.re, y.im);
+    }
+  }
+  __syncthreads();
+
+  // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
+  if (tid < kPairs * 20) {
+    const int p = tid / 20, k1 = tid % 20;
+    cpx x[20];
+#pragma unroll
+    for (int n2 = 0; n2 < 20; ++n2) {
+      const float2 v = sm.u.t[p][k1][n2];
+      x[n2] = {v.x, v.y};
+    }
+    dft20(x);
+#pragma unroll
+    for (int k2 = 0; k2 < 20; ++k2) sm.z[p][k1 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
+  }
+  __syncthreads();
+
+  // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
+  for (int i = tid; i < kPairs * kBins; i += kThreads) {
+    const int p = i / kBins, k = i % kBins;
+    const float2 a = sm.z[p][k];
+    const float2 b = sm.z[p][k == 0 ? 0 : 400 - k];
+    const float ar = a.x + b.x, ai = a.y - b.y;
+    const float br = a.x - b.x, bi = a.y + b.y;
+    sm.u.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
+    sm.u.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
+  }
+  __syncthreads();
+
+  // ---- mel projection + log10, tile maximum
+  float local_max = -INFINITY;
+  float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0;
+  for (int i = tid; i < kMel * kTileFrames; i += kThreads) {
+    const int m = i / kTileFrames, f = i % kTileFrames;
+    const int lo = sm.mel_lo[m];
+    const int beg = sm.mel_off[m], end = sm.mel_off[m + 1];
+    const float* pw = sm.u.p[f] + lo - beg;
+    float acc = 0.f;
+    for (int q = beg; q < end; ++q) acc += sm.melw[q] * pw[q];
+    const float v = log10f(fmaxf(acc, 1e-10f));
+    dst[static_cast<int64_t>(m) * kFrames + f] = v;
+    local_max = fmaxf(local_max, v);
+  }
+  local_max = warp_max(local_max);
+  if ((tid & 31) == 0) sm.red[tid >> 5] = local_max;
+  __syncthreads();
+  if (tid == 0) {
+    float mx = sm.red[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) mx = fmaxf(mx, sm.red[w]);
+    tile_max[chunk * kTilesPerChunk + tile] = mx;
+  }
+}
+
+// Fold the chunk's tile maxima, then out = (max(x, max - 8) + 4) / 4 over a
+// slice of the chunk.  The slice was written by mel_tile_kernel moments
+// before and is read from L2.
+__global__ void __launch_bounds__(kThreads)
+    mel_normalize_kernel(float* __restrict__ out, const float* __restrict__ tile_max,
+                         int chunk0) {
+  __shared__ float red[kThreads / 32];
+  const int tid = threadIdx.x;
+  const int64_t chunk = chunk0 + blockIdx.y;
+  float mx = -INFINITY;
+  for (int i = tid; i < kTilesPerChunk; i += kThreads)
+    mx = fmaxf(mx, __ldcg(tile_max + chunk * kTilesPerChunk + i));
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  const float floor_log = mx - 8.0f;
+
+  constexpr int kVec4PerChunk = kMel * kFrames / 4;  // 96000
+  constexpr int kPerSlice = kVec4PerChunk / kNormSlices;  // 6000
+  float4* base = reinterpret_cast<float4*>(out + chunk * (static_cast<int64_t>(kMel) * kFrames)) +
+                 blockIdx.x * kPerSlice;
+  for (int i = tid; i < kPerSlice; i += kThreads) {
+    float4 v = __ldcg(base + i);
+    v.x = (fmaxf(v.x, floor_log) + 4.0f) / 4.0f;
+    v.y = (fmaxf(v.y, floor_log) + 4.0f) / 4.0f;
+    v.z = (fmaxf(v.z, floor_log) + 4.0f) / 4.0f;
+    v.w = (fmaxf(v.w, floor_log) + 4.0f) / 4.0f;
+    __stcs(base + i, v);
+  }
+}
+
+// Opt the tile kernel into > 48 KB of dynamic shared memory, once per device.
+cudaError_t enable_large_smem(size_t smem) {
+  static std::atomic<int> done[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  err = cudaFuncSetAttribute(mel_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+  if (err == cudaSuccess && dev >= 0 && dev < 64) done[dev].store(1, std::memory_order_release);
+  return err;
+}
+
+}  // namespace
+
+size_t logmel_workspace_bytes(int64_t chunks) {
+  const size_t raw = static_cast<size_t>(chunks) * kTilesPerChunk * sizeof(float);
+  return (raw + 255) & ~static_cast<size_t>(255);
+}
+
+cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
+                          cudaStream_t stream) {
+  static_assert(sizeof(MelSmem) <= 113 * 1024, "two tiles must fit one SM");
+  const size_t smem = sizeof(MelSmem);
+  cudaError_t err = enable_large_smem(smem);
+  if (err != cudaSuccess) return err;
+  for (int64_t c0 = 0; c0 < chunks; c0 += kBatchChunks) {
+    const int64_t n = chunks - c0 < kBatchChunks ? chunks - c0 : kBatchChunks;
+    mel_tile_kernel<<<dim3(kTilesPerChunk, static_cast<unsigned>(n)), kThreads, smem, stream>>>(
+        pcm, out, tile_max, static_cast<int>(c0));
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    mel_normalize_kernel<<<dim3(kNormSlices, static_cast<unsigned>(n)), kThreads, 0, stream>>>(
+        out, tile_max, static_cast<int>(c0));
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace vl

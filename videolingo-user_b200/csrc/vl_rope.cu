@@ -1,0 +1,167 @@
+// Rotate-half rotary embedding applied in place to Q/K, and its decode-step
+// fusion with the KV-cache append, for sm_100a.
+//
+// Reference semantics (VideoLingo-user native/asr/src):
+//   rope_kernel (engine.cu:214-233) + build_rope_table (engine.cu:892-905)
+//   rope_full / rope_rows / rope_at_position(_dev/_map) kernels
+//   (decoder.cu:113-134, 307-333, 471-498, 670-695, 789-814)
+//   + build_full_rope_table (decoder.cu:950-961)
+//       inv_freq(d) = 1/pow(base, 2d/rot) (fp64), angle = inv_freq * pos (fp64),
+//       cos/sin rounded to fp32;  x1' = x1*c - x2*s, x2' = x2*c + x1*s
+//       over the pairs (d, d + rot/2), d < rot/2, of every head.
+// The reference reads cos/sin from host-built tables of 1024 or 1500 rows;
+// here they are evaluated per (token, pair) in fp64 on the device (no table,
+// no position limit) and shared through shared memory by all heads of the
+// token.  Each thread then rotates one 16-byte vector of x1 together with
+// the matching vector of x2, so every head's rotated half moves as whole
+// 16-byte accesses and the untouched half is never read.
+#include <cmath>
+
+#include "vl_common.cuh"
+#include "vl_kernels.h"
+
+namespace vl {
+namespace {
+
+constexpr int kRopeThreads = 128;
+constexpr int kMaxHalfRot = 128;
+constexpr int kMaxTokensPerBlock = 8;
+
+struct InvFreq {
+  double v[kMaxHalfRot];
+};
+
+__device__ __forceinline__ int64_t token_position(const RopeArgs& a, int64_t r) {
+  if (a.positions == nullptr) return a.pos_offset + (a.seq_len > 0 ? r % a.seq_len : r);
+  const int64_t src = a.row_map ? static_cast<int64_t>(a.row_map[r]) : r;
+  return a.pos_offset + static_cast<int64_t>(a.positions[src * a.positions_stride]);
+}
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kRopeThreads)
+    rope_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq, int tokens_per_block) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  extern __shared__ float2 cs[];  // [tokens_per_block][half_rot] (cos, sin)
+  const int half_rot = a.rotary_dim / 2;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tokens_per_block;
+  int nt = tokens_per_block;
+  if (t0 + nt > a.tokens) nt = static_cast<int>(a.tokens - t0);
+
+  for (int i = threadIdx.x; i < nt * half_rot; i += kRopeThreads) {
+    const int t = i / half_rot, d = i % half_rot;
+    const double angle = static_cast<double>(token_position(a, t0 + t)) * freq.v[d];
+    double s, c;
+    sincos(angle, &s, &c);
+    cs[i] = make_float2(static_cast<float>(c), static_cast<float>(s));
+  }
+  __syncthreads();
+
+  const int heads = a.n_q_heads + a.n_k_heads;
+  const int per_head = kVec ? half_rot / E : half_rot;
+  const int tasks = heads * per_head;
+  for (int i = threadIdx.x; i < nt * tasks; i += kRopeThreads) {
+    const int t = i / tasks;
+    const int rem = i % tasks;
+    const int h = rem / per_head, j = rem % per_head;
+    const int64_t r = t0 + t;
+    T* head = h < a.n_q_heads
+                  ? static_cast<T*>(a.q) + r * a.q_row_stride + static_cast<int64_t>(h) * a.head_dim
+                  : static_cast<T*>(a.k) + r * a.k_row_stride +
+                        static_cast<int64_t>(h - a.n_q_heads) * a.head_dim;
+    const float2* cst = cs + t * half_rot;
+    if (kVec) {
+      uint4* p1 = reinterpret_cast<uint4*>(head + j * E);
+      uint4* p2 = reinterpret_cast<uint4*>(head + half_rot + j * E);
+      float x1[E], x2[E], y1[E], y2[E];
+      S::unpack(ld_vec(p1), x1);
+      S::unpack(ld_vec(p2), x2);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float c = cst[j * E + e].x, s = cst[j * E + e].y;
+        y1[e] = x1[e] * c - x2[e] * s;
+        y2[e] = x2[e] * c + x1[e] * s;
+      }
+      st_vec(p1, S::pack(y1));
+      st_vec(p2, S::pack(y2));
+    } else {
+      const float c = cst[j].x, s = cst[j].y;
+      const float x1 = S::to_float(head[j]);
+      const float x2 = S::to_float(head[j + half_rot]);
+      head[j] = S::from_float(x1 * c - x2 * s);
+      head[j + half_rot] = S::from_float(x2 * c + x1 * s);
+    }
+  }
+
+  if (a.v == nullptr) return;
+  // Fused KV append: the rotated K rows written above are visible to the
+  // whole block after the barrier; copy them and the V rows to their slots.
+  __syncthreads();
+  const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
+  const int64_t vec_per_row = kVec ? row_elems / E : row_elems;
+  for (int64_t i = threadIdx.x; i < nt * vec_per_row; i += kRopeThreads) {
+    const int t = static_cast<int>(i / vec_per_row);
+    const int64_t c = i % vec_per_row;
+    const int64_t r = t0 + t;
+    const int64_t slot = a.slot_mapping[r];
+    if (slot < 0) continue;
+    if (slot >= a.num_slots) {
+      if (c == 0 && a.status) atomicOr(a.status, VL_STATUS_BAD_SLOT);
+      continue;
+    }
+    const T* krow = static_cast<const T*>(a.k) + r * a.k_row_stride;
+    const T* vrow = static_cast<const T*>(a.v) + r * row_elems;
+    T* kc = static_cast<T*>(a.k_cache) + slot * row_elems;
+    T* vc = static_cast<T*>(a.v_cache) + slot * row_elems;
+    if (kVec) {
+      st_vec(reinterpret_cast<uint4*>(kc) + c, ld_vec(reinterpret_cast<const uint4*>(krow) + c));
+      st_vec(reinterpret_cast<uint4*>(vc) + c, ld_vec(reinterpret_cast<const uint4*>(vrow) + c));
+    } else {
+      kc[c] = krow[c];
+      vc[c] = vrow[c];
+    }
+  }
+}
+
+template <typename T>
+cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
+  constexpr int E = Storage<T>::kVec;
+  const int half_rot = a.rotary_dim / 2;
+  InvFreq freq;
+  for (int d = 0; d < half_rot; ++d)
+    freq.v[d] = 1.0 / std::pow(a.base, static_cast<double>(2 * d) / a.rotary_dim);
+  const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
+  bool vec = half_rot % E == 0 && a.head_dim % E == 0 && aligned16(a.q) &&
+             a.q_row_stride % E == 0 &&
+             (a.n_k_heads == 0 || (aligned16(a.k) && a.k_row_stride % E == 0));
+  if (a.v != nullptr)
+    vec = vec && aligned16(a.v) && aligned16(a.k_cache) && aligned16(a.v_cache) &&
+          row_elems % E == 0;
+  // Enough blocks to cover the SMs several times, up to 8 tokens per block.
+  const int64_t want_blocks = static_cast<int64_t>(sm_count()) * 4;
+  int64_t tpb = (a.tokens + want_blocks - 1) / want_blocks;
+  if (tpb < 1) tpb = 1;
+  if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;
+  const int64_t blocks = (a.tokens + tpb - 1) / tpb;
+  const size_t smem = static_cast<size_t>(tpb) * half_rot * sizeof(float2);
+  if (vec)
+    rope_kernel<T, true><<<static_cast<unsigned>(blocks), kRopeThreads, smem, stream>>>(
+        a, freq, static_cast<int>(tpb));
+  else
+    rope_kernel<T, false><<<static_cast<unsigned>(blocks), kRopeThreads, smem, stream>>>(
+        a, freq, static_cast<int>(tpb));
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_rope(const RopeArgs& args, int dtype, cudaStream_t stream) {
+  if (args.tokens == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtypeF32: return rope_typed<float>(args, stream);
+    case kDtypeF16: return rope_typed<__half>(args, stream);
+    default: return rope_typed<__nv_bfloat16>(args, stream);
+  }
+}
+
+}  // namespace vl

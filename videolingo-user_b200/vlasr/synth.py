@@ -1,0 +1,64 @@
+"""Seeded synthetic inputs with the shapes and value distributions of the
+benchmark configurations (no real audio or checkpoint is needed).
+
+* audio chunks: 30 s of 16 kHz mono f32 = sum of 8 sinusoids (frequency
+  U(80, 4000) Hz, amplitude U(0, 0.1), phase U(0, 2pi)) + N(0, 0.01) noise,
+  clipped to [-1, 1]; one independent seed per chunk.
+* activations N(0, 1), LayerNorm gamma N(1, 0.02), beta N(0, 0.02), RMSNorm
+  weight N(1, 0.02), embedding table N(0, 0.02), token ids U[0, vocab).
+
+The reference's own mel test signal (three sines plus 0.05*N(0,1),
+tests/test_native_asr_m0.py:143-154 of VideoLingo-user) is `tone_pcm`.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+SAMPLE_RATE = 16000
+CHUNK_SAMPLES = 480000
+
+
+def audio_chunk(seed: int, samples: int = CHUNK_SAMPLES) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    freqs = rng.uniform(80.0, 4000.0, size=8)
+    amps = rng.uniform(0.0, 0.1, size=8)
+    phases = rng.uniform(0.0, 2.0 * np.pi, size=8)
+    t = np.arange(samples, dtype=np.float64) / SAMPLE_RATE
+    x = (amps[:, None] * np.sin(2.0 * np.pi * freqs[:, None] * t[None, :] + phases[:, None])).sum(0)
+    x += rng.normal(0.0, 0.01, size=samples)
+    return np.clip(x, -1.0, 1.0).astype(np.float32)
+
+
+def audio_chunks(chunks: int, seed: int = 0, samples: int = CHUNK_SAMPLES) -> np.ndarray:
+    """[chunks, samples] f32, chunk c seeded with seed*100003 + c."""
+    out = np.empty((chunks, samples), dtype=np.float32)
+    for c in range(chunks):
+        out[c] = audio_chunk(seed * 100003 + c, samples)
+    return out
+
+
+def tone_pcm(sample_count: int, seed: int = 42) -> np.ndarray:
+    """440/1234/3000 Hz sines + 0.05*N(0,1) (the reference mel test signal)."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(sample_count, dtype=np.float64)
+    signal = (0.3 * np.sin(2 * np.pi * 440 * t / 16000)
+              + 0.2 * np.sin(2 * np.pi * 1234 * t / 16000)
+              + 0.1 * np.sin(2 * np.pi * 3000 * t / 16000)
+              + 0.05 * rng.standard_normal(sample_count))
+    return signal.astype(np.float32)
+
+
+def pad_chunk(pcm: np.ndarray) -> np.ndarray:
+    """Zero-pad (or reject) a clip to one 30 s chunk, as the reference CLI does
+    (native/asr/src/main_m0.cu:60-79)."""
+    if pcm.size > CHUNK_SAMPLES:
+        raise ValueError("PCM exceeds the 30 s chunk (480000 samples)")
+    out = np.zeros(CHUNK_SAMPLES, dtype=np.float32)
+    out[:pcm.size] = pcm
+    return out
+
+
+def normal(shape, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return rng.normal(mean, std, size=shape).astype(np.float32)
