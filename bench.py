@@ -1,0 +1,482 @@
+"""Benchmark of the B200 hot path (the box-scale configuration).
+
+Workload: 256 independent 30 s chunks of seeded
+synthetic audio (8 sinusoids + noise) -> log-mel frontend -> 32 layers x
+(fused residual-add + LayerNorm on [1500, 1280] bf16, exact-erf GELU on
+[1500, 5120] bf16) per chunk; chunks are sharded over the ranks (strong
+scaling: 256 / N chunks each) and the [256, 1500, 1280] bf16 outputs are
+all-gathered over NCCL when N > 1.  Metric: audio seconds processed per
+second (whole job).  Also reported: per-op HBM throughput on each op's
+largest configuration (configs 1-3) as a fraction of the measured HBM peak.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "videolingo-user_b200"))
+sys.path.insert(0, str(ROOT))
+
+TOTAL_CHUNKS = 256
+LAYERS = 32
+AUDIO_SECONDS_PER_CHUNK = 30.0
+METRIC = "audio-seconds/s (log-mel + 32 x fused add+LayerNorm & GELU per 30 s chunk)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--chunks", type=int, default=TOTAL_CHUNKS)
+    p.add_argument("--no-ops", action="store_true", help="skip the per-op roofline table")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) timing")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return p.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def init_dist(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# per-op table (configs 1-3 and the mel at 256 chunks), rank 0 only
+# ---------------------------------------------------------------------------
+
+def time_op(fn, iters: int, flush=None) -> float:
+    """Mean device time (ms) of fn over `iters` launches, L2 flushed before each."""
+    import torch
+    s = torch.cuda.current_stream()
+    total = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        fn()
+        b.record(s)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / iters
+
+
+def op_table(peak: float) -> dict:
+    import torch
+    import vlasr
+    dev = torch.device("cuda")
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1234)
+    flush_buf = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)  # noqa: E731  (larger than the 126 MB L2)
+
+    def rnd(shape, mean=0.0, std=1.0, dtype=bf):
+        t = torch.empty(shape, device=dev, dtype=torch.float32)
+        t.normal_(mean, std, generator=g)
+        return t.to(dtype)
+
+    rows = {}
+
+    def add(name, config, nbytes, fn, iters=20, latency=False):
+        fn()
+        torch.cuda.synchronize()
+        ms = time_op(fn, iters, flush)
+        entry = {"config": config, "bytes": nbytes, "us": round(ms * 1e3, 2)}
+        if not latency:
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            entry.update({"gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 3)})
+        rows[name] = entry
+
+    # config 1
+    x, r = rnd((8 * 1500, 1280)), rnd((8 * 1500, 1280))
+    gam, bet = rnd(1280, 1.0, 0.02), rnd(1280, 0.0, 0.02)
+    out = torch.empty_like(x)
+    add("add_layernorm", "[8,1500,1280] bf16", 4 * x.numel() * 2,
+        lambda: vlasr.add_layernorm(r, x, gam, bet, out=out))
+    del x, r, out
+    gi = rnd((8 * 1500, 5120))
+    go = torch.empty_like(gi)
+    add("gelu_erf", "[8,1500,5120] bf16", 2 * gi.numel() * 2, lambda: vlasr.gelu_erf(gi, out=go))
+    del gi, go
+    # config 2
+    table = rnd((151552, 2048), 0.0, 0.02)
+    ids = torch.randint(0, 151552, (4, 2048), device=dev, generator=g)
+    eo = torch.empty(4, 2048, 2048, dtype=bf, device=dev)
+    add("embed_gather", "ids [4,2048] from [151552,2048] bf16", 2 * eo.numel() * 2 + ids.numel() * 8,
+        lambda: vlasr.embed_gather(ids, table, out=eo))
+    del table, eo
+    x, r, w = rnd((4 * 2048, 2048)), rnd((4 * 2048, 2048)), rnd(2048, 1.0, 0.02)
+    out = torch.empty_like(x)
+    add("add_rmsnorm", "[4,2048,2048] bf16", 4 * x.numel() * 2,
+        lambda: vlasr.add_rmsnorm(r, x, w, out=out))
+    del x, r, out
+    gt, up = rnd((4 * 2048, 6144)), rnd((4 * 2048, 6144))
+    so = torch.empty_like(gt)
+    add("swiglu", "gate/up [4,2048,6144] bf16", 3 * gt.numel() * 2,
+        lambda: vlasr.swiglu(gt, up, out=so))
+    del gt, up, so
+    q, k = rnd((4, 2048, 16, 128)), rnd((4, 2048, 4, 128))
+    add("rope", "Q [4,2048,16,128] K [4,2048,4,128] rot 64", (q.numel() + k.numel()) * 2 // 2 * 2,
+        lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, seq_len=2048))
+    del q, k
+    # mel: one chunk (latency) and 256 chunks (throughput)
+    from vlasr.synth import audio_chunks_device
+    pcm = audio_chunks_device(256, 0, 7, dev)
+    mel = torch.empty(256, 128, 3000, device=dev)
+    ws = torch.empty(vlasr.logmel_workspace_bytes(256), dtype=torch.uint8, device=dev)
+    add("logmel", "256 x 30 s chunks", 256 * 3456000,
+        lambda: vlasr.logmel(pcm, out=mel, workspace=ws), iters=5)
+    add("logmel_1chunk", "1 x 30 s chunk", 3456000,
+        lambda: vlasr.logmel(pcm[:1], out=mel[:1], workspace=ws), iters=20)
+    del pcm, mel
+    # config 3: decode step (latency-bound)
+    x, r, w = rnd((64, 2048)), rnd((64, 2048)), rnd(2048, 1.0, 0.02)
+    out = torch.empty_like(x)
+    add("decode_add_rmsnorm", "[64,2048] bf16", 4 * x.numel() * 2,
+        lambda: vlasr.add_rmsnorm(r, x, w, out=out), latency=True)
+    q, k, v = rnd((64, 16, 128)), rnd((64, 4, 128)), rnd((64, 4, 128))
+    kc = torch.zeros(64 * 4096, 4, 128, dtype=bf, device=dev)
+    vc = torch.zeros_like(kc)
+    pos = torch.randint(0, 4096, (64,), device=dev, generator=g, dtype=torch.int64)
+    slots = torch.arange(64, device=dev) * 4096 + pos
+    pos32 = pos.to(torch.int32)
+    add("decode_rope", "Q [64,16,128] K [64,4,128] rot 64", (q.numel() + k.numel()) * 2,
+        lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, positions=pos32), latency=True)
+    add("decode_kv_append", "K/V [64,4,128] -> 64x4096 slots", 4 * k.numel() * 2,
+        lambda: vlasr.kv_append(k, v, kc, vc, slots), latency=True)
+    add("decode_rope_kv_append", "fused RoPE + KV append", (q.numel() + 3 * k.numel()) * 2,
+        lambda: vlasr.rope_kv_append(q, k, v, kc, vc, pos32, slots, head_dim=128, rotary_dim=64),
+        latency=True)
+    del flush_buf
+    torch.cuda.empty_cache()
+    return rows
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's CPU implementation on a bounded sample
+# ---------------------------------------------------------------------------
+
+def cpu_baseline(target_s: float = 12.0) -> dict:
+    from oracle import cpu_reference
+    threads = os.cpu_count() or 1
+    pilot = cpu_reference.time_sample(2, layers=LAYERS, seed=1, threads=threads)
+    per_chunk = pilot["total_s"] / 2
+    chunks = int(max(2, min(96, target_s / max(per_chunk, 1e-3))))
+    res = cpu_reference.time_sample(chunks, layers=LAYERS, seed=2, threads=threads)
+    value = chunks * AUDIO_SECONDS_PER_CHUNK / res["total_s"]
+    return {"value": round(value, 2), "unit": "audio-s/s", "cores": threads, "kind": "reference",
+            "sample": (f"{chunks} chunks of the box-scale workload on the host CPU: transformers "
+                       f"WhisperFeatureExtractor (torch path) + 32 x torch-CPU bf16 add+layer_norm "
+                       f"& gelu; mel {res['mel_s']:.2f} s, layers {res['layers_s']:.2f} s"),
+            "seconds": round(res["total_s"], 2)}
+
+
+def run_reference_arm(args) -> None:
+    """`--impl reference`: the reference's CPU path on this box (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_reference
+    threads = os.cpu_count() or 1
+    chunks = 4
+    for _ in range(args.warmup):
+        cpu_reference.time_sample(chunks, layers=LAYERS, seed=0, threads=threads)
+    times = []
+    for i in range(args.steps):
+        times.append(cpu_reference.time_sample(chunks, layers=LAYERS, seed=i + 1,
+                                               threads=threads)["total_s"])
+    per_step = sum(times) / len(times)
+    value = chunks * AUDIO_SECONDS_PER_CHUNK / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "audio-s/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "box-scale chain (config 4), bounded CPU sample",
+                   "chunks_per_step": chunks, "layers": LAYERS,
+                   "path": "transformers WhisperFeatureExtractor + torch CPU layer_norm/gelu"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "audio-s/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{chunks} chunks per step, {args.steps} steps"},
+        "e2e": {"value": round(value, 2), "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# main arm
+# ---------------------------------------------------------------------------
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    import torch
+    import vlasr
+    from vlasr.pipeline import ChainShape, EncoderNormChain, shard_range
+    from vlasr.synth import audio_chunks_device
+
+    world, rank, local = init_dist(args)
+    dev = torch.device("cuda", local)
+    vlasr.load()
+    peak, peak_kind = peaks()
+    c0, c1 = shard_range(args.chunks, rank, world)
+    shape = ChainShape(chunks=c1 - c0, layers=LAYERS)
+    group = None
+    chain = EncoderNormChain(shape, dev, seed=0, group=group, world=world, rank=rank,
+                             total_chunks=args.chunks)
+    pcm = audio_chunks_device(shape.chunks, c0, 0, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # per-launch CUDA events for the kernel breakdown inside the timed region
+    events: dict[str, list] = {}
+
+    def timer(name, fn):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        events.setdefault(name, []).append((a, b))
+
+    for _ in range(args.warmup):
+        chain.step(pcm)
+    torch.cuda.synchronize()
+    barrier(world)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        chain.step(pcm, timer=timer)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    elapsed_ms = max_over_ranks(t0.elapsed_time(t1), world)
+    ms_per_step = elapsed_ms / args.steps
+    audio_s = args.chunks * AUDIO_SECONDS_PER_CHUNK
+    value = audio_s / (ms_per_step / 1e3)
+
+    breakdown = {}
+    for name, pairs in events.items():
+        tot = sum(a.elapsed_time(b) for a, b in pairs)
+        breakdown[name] = {"launches": len(pairs), "mean_us": round(tot / len(pairs) * 1e3, 2),
+                           "share": round(tot / elapsed_ms, 4)}
+    bytes_step = shape.bytes_per_step()
+    gelu_us = breakdown["gelu"]["mean_us"]
+    gelu_gbs = bytes_step["gelu"] / (gelu_us * 1e-6) / 1e9
+    traffic = None
+    tpath = ROOT / "profiles" / "traffic.json"
+    if tpath.exists():
+        try:
+            per_row = json.loads(tpath.read_text())["gelu_erf"]["dram_bytes_per_row"]
+            traffic = int(per_row * shape.rows)
+        except Exception:  # noqa: BLE001
+            traffic = None
+    roofline = {"bound": "hbm", "kernel": "gelu_erf (vl_gelu_erf)", "achieved": round(gelu_gbs, 1),
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round(gelu_gbs / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": bytes_step["gelu"]}
+    for name in ("add_layernorm", "mel"):
+        if name in breakdown:
+            us = breakdown[name]["mean_us"]
+            breakdown[name]["gbs"] = round(bytes_step[name] / (us * 1e-6) / 1e9, 1)
+            breakdown[name]["frac_of_peak"] = round(bytes_step[name] / (us * 1e-6) / 1e9 / peak, 4)
+    breakdown["gelu"]["gbs"] = round(gelu_gbs, 1)
+    breakdown["gelu"]["frac_of_peak"] = round(gelu_gbs / peak, 4)
+    launches = chain.launches_per_step() * args.steps
+
+    # e2e through the host-buffer API (pinned PCM in, pinned mel + outputs back)
+    e2e = None
+    if not args.no_e2e:
+        pcm_host = pcm.cpu().pin_memory()
+        mel_host = torch.empty((shape.chunks, 128, 3000), dtype=torch.float32).pin_memory()
+        y_host = torch.empty((shape.rows, shape.hidden), dtype=torch.bfloat16).pin_memory()
+        pcm_dev = torch.empty_like(pcm)
+        groups = max(1, min(8, shape.chunks // 8))
+        for _ in range(max(1, args.warmup)):
+            chain.step_host(pcm_host, mel_host, y_host, pcm_dev, groups=groups)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            chain.step_host(pcm_host, mel_host, y_host, pcm_dev, groups=groups)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+        h2d, d2h = chain.host_bytes_per_step()
+        e2e = {"value": round(audio_s / (e_ms / 1e3), 1), "unit": "audio-s/s",
+               "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
+               "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)), "groups": groups,
+               "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)"}
+        del pcm_host, mel_host, y_host, pcm_dev
+
+    del chain, pcm
+    torch.cuda.empty_cache()
+    ops = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_ops:
+            ops = op_table(peak)
+        if not args.no_cpu:
+            cpu = cpu_baseline()
+    barrier(world)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded 8-sinusoid audio, N(0,1) activations, seeded weights)",
+            "config": {"workload": "config 4: box-scale chunk sharding", "chunks": args.chunks,
+                       "chunks_per_rank": shape.chunks, "layers": LAYERS,
+                       "ln_shape": [1500, 1280], "gelu_shape": [1500, 5120],
+                       "parallelism": f"chunk-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "l2": "inputs larger than L2 (each op streams >= 0.49 GB per launch)",
+                       "bytes_per_step": bytes_step["total"] * world},
+            "roofline": roofline, "kernels": breakdown, "gpu_launches": launches,
+            "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "ops": ops,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

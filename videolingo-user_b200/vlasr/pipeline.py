@@ -1,0 +1,194 @@
+"""Chunk pipeline of the box-scale configuration: log-mel frontend, then
+`layers` x (fused residual-add + LayerNorm on [frames, hidden] and exact-erf
+GELU on [frames, ffn]) per 30 s chunk, optionally sharded by chunk over the
+ranks of a process group with one all-gather of the encoder-norm outputs.
+
+This is the part of the reference's encoder stage that the fused ops cover
+(VideoLingo-user native/asr/src/engine.cu:1341-1578 - layer_norm, residual
+add, GELU per layer - and mel_frontend.cu:209-291).  The contractions
+between them (attention, fc1/fc2 GEMMs, conv frontend) are outside this
+library, so each layer's inputs stand in for their outputs: the LayerNorm
+residual stream is a seeded [frames, hidden] state per chunk whose delta is
+the previous layer's normalised output, and the GELU input is a seeded
+[frames, ffn] buffer per chunk, as the benchmark configuration prescribes.
+
+Two entry points:
+* `step()`      - device-resident inputs (HBM throughput of the ops);
+* `step_host()` - host PCM in, host mel + encoder-norm outputs out, pipelined
+  over chunk groups on three streams so H2D, kernels and D2H overlap.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops
+from .synth import CHUNK_SAMPLES
+
+FRAMES = 1500
+HIDDEN = 1280
+FFN = 5120
+MEL_BINS = 128
+MEL_FRAMES = 3000
+
+
+@dataclass
+class ChainShape:
+    chunks: int                 # chunks processed by this rank
+    layers: int = 32
+    frames: int = FRAMES
+    hidden: int = HIDDEN
+    ffn: int = FFN
+
+    @property
+    def rows(self) -> int:
+        return self.chunks * self.frames
+
+    def bytes_per_step(self) -> dict:
+        """Algorithmic HBM bytes (read every input once, write every output once)."""
+        mel = self.chunks * (CHUNK_SAMPLES * 4 + MEL_BINS * MEL_FRAMES * 4)
+        ln = 4 * self.rows * self.hidden * 2            # residual, delta in; residual, out
+        gelu = 2 * self.rows * self.ffn * 2             # in, out
+        return {"mel": mel, "add_layernorm": ln, "gelu": gelu,
+                "total": mel + self.layers * (ln + gelu)}
+
+
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous chunk range [begin, end) of `rank`; equal shares when world divides total."""
+    base, extra = divmod(total, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+class EncoderNormChain:
+    """Resident buffers and launch sequence of one rank's shard."""
+
+    def __init__(self, shape: ChainShape, device, seed: int = 0, group=None, world: int = 1,
+                 rank: int = 0, total_chunks: int | None = None):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.group = group
+        self.world = world
+        self.rank = rank
+        self.total_chunks = total_chunks if total_chunks is not None else shape.chunks * world
+        s = shape
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed * 7919 + rank)
+        bf = torch.bfloat16
+
+        def normal(shape_, mean=0.0, std=1.0):
+            t = torch.empty(shape_, device=self.device, dtype=torch.float32)
+            t.normal_(mean, std, generator=gen)
+            return t.to(bf)
+
+        self.gamma = normal((s.layers, s.hidden), 1.0, 0.02)
+        self.beta = normal((s.layers, s.hidden), 0.0, 0.02)
+        self.h = normal((s.rows, s.hidden))          # residual stream
+        self.y = normal((s.rows, s.hidden))          # LN output = next layer's delta
+        self.g_in = normal((s.rows, s.ffn))          # FFN hidden (stand-in for fc1 output)
+        self.g_out = torch.empty((s.rows, s.ffn), device=self.device, dtype=bf)
+        self.mel = torch.empty((s.chunks, MEL_BINS, MEL_FRAMES), device=self.device,
+                               dtype=torch.float32)
+        self.mel_ws = torch.empty(ops.logmel_workspace_bytes(max(s.chunks, 1)), device=self.device,
+                                  dtype=torch.uint8)
+        self.y_all = None
+        if world > 1:
+            self.y_all = torch.empty((self.total_chunks * s.frames, s.hidden), device=self.device,
+                                     dtype=bf)
+
+    # -- launch sequences ---------------------------------------------------
+    def launches_per_step(self, groups: int = 1) -> int:
+        """Kernels of this library launched by one step (mel: 2 per 32-chunk batch)."""
+        per_group = math.ceil(self.shape.chunks / groups)
+        mel = 0
+        left = self.shape.chunks
+        while left > 0:
+            n = min(per_group, left)
+            mel += 2 * math.ceil(n / 32)
+            left -= n
+        return mel + 2 * self.shape.layers * groups
+
+    def run_mel(self, pcm: torch.Tensor, c0: int = 0, c1: int | None = None) -> None:
+        c1 = self.shape.chunks if c1 is None else c1
+        ops.logmel(pcm[c0:c1], out=self.mel[c0:c1], workspace=self.mel_ws)
+
+    def run_layer(self, l: int, r0: int = 0, r1: int | None = None) -> None:
+        r1 = self.shape.rows if r1 is None else r1
+        y = self.y[r0:r1]
+        ops.add_layernorm(self.h[r0:r1], y, self.gamma[l], self.beta[l], out=y)
+        ops.gelu_erf(self.g_in[r0:r1], out=self.g_out[r0:r1])
+
+    def all_gather(self) -> None:
+        if self.y_all is not None:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(self.y_all, self.y, group=self.group)
+
+    def step(self, pcm: torch.Tensor, timer=None) -> None:
+        """One pass over this rank's chunks with device-resident PCM.
+
+        `timer(name, fn)` (optional) wraps each launch, e.g. with CUDA events."""
+        call = timer if timer is not None else (lambda name, fn: fn())
+        call("mel", lambda: self.run_mel(pcm))
+        for l in range(self.shape.layers):
+            call("add_layernorm", lambda l=l: ops.add_layernorm(
+                self.h, self.y, self.gamma[l], self.beta[l], out=self.y))
+            call("gelu", lambda: ops.gelu_erf(self.g_in, out=self.g_out))
+        if self.world > 1:
+            call("all_gather", self.all_gather)
+
+    # -- host-buffer path -----------------------------------------------------
+    def step_host(self, pcm_host: torch.Tensor, mel_host: torch.Tensor, y_host: torch.Tensor,
+                  pcm_dev: torch.Tensor, groups: int = 4) -> None:
+        """Host PCM [chunks, 480000] -> host mel [chunks,128,3000] and host
+        encoder-norm outputs [chunks*frames, hidden] (pinned buffers).
+
+        Chunk groups flow through three streams: group g+1's PCM uploads while
+        group g computes and group g-1's results download."""
+        s = self.shape
+        cur = torch.cuda.current_stream(self.device)
+        up = torch.cuda.Stream(self.device)
+        down = torch.cuda.Stream(self.device)
+        bounds = [shard_range(s.chunks, g, groups) for g in range(groups)]
+        bounds = [b for b in bounds if b[1] > b[0]]
+        uploaded = []
+        up.wait_stream(cur)
+        with torch.cuda.stream(up):
+            for c0, c1 in bounds:
+                pcm_dev[c0:c1].copy_(pcm_host[c0:c1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(up)
+                uploaded.append(ev)
+        for (c0, c1), ev in zip(bounds, uploaded):
+            cur.wait_event(ev)
+            self.run_mel(pcm_dev, c0, c1)
+            r0, r1 = c0 * s.frames, c1 * s.frames
+            for l in range(s.layers):
+                self.run_layer(l, r0, r1)
+            done = torch.cuda.Event()
+            done.record(cur)
+            down.wait_event(done)
+            with torch.cuda.stream(down):
+                mel_host[c0:c1].copy_(self.mel[c0:c1], non_blocking=True)
+                y_host[r0:r1].copy_(self.y[r0:r1], non_blocking=True)
+        if self.world > 1:
+            self.all_gather()
+        cur.wait_stream(down)
+
+    def host_bytes_per_step(self) -> tuple[int, int]:
+        s = self.shape
+        h2d = s.chunks * CHUNK_SAMPLES * 4
+        d2h = s.chunks * MEL_BINS * MEL_FRAMES * 4 + s.rows * s.hidden * 2
+        return h2d, d2h
+
+
+def seeded_pcm(chunks: int, first_chunk: int, seed: int = 0) -> np.ndarray:
+    """[chunks, 480000] f32 seeded audio for global chunks first_chunk.. (config 0 recipe)."""
+    from .synth import audio_chunk
+    out = np.empty((chunks, CHUNK_SAMPLES), dtype=np.float32)
+    for i in range(chunks):
+        out[i] = audio_chunk(seed * 100003 + first_chunk + i)
+    return out

@@ -62,3 +62,30 @@ def pad_chunk(pcm: np.ndarray) -> np.ndarray:
 def normal(shape, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return rng.normal(mean, std, size=shape).astype(np.float32)
+
+
+def audio_chunks_device(chunks: int, first_chunk: int, seed: int, device):
+    """[chunks, 480000] f32 torch tensor on `device` with the audio_chunk
+    recipe: sinusoid parameters drawn per chunk from numpy exactly as
+    audio_chunk does, the sum evaluated in fp64 on the device, and
+    N(0, 0.01) noise from a seeded torch generator (fast for hundreds of
+    chunks; the noise differs from audio_chunk's numpy stream)."""
+    import torch
+    params = np.empty((chunks, 3, 8), dtype=np.float64)
+    for i in range(chunks):
+        rng = np.random.default_rng(seed * 100003 + first_chunk + i)
+        params[i, 0] = rng.uniform(80.0, 4000.0, size=8)
+        params[i, 1] = rng.uniform(0.0, 0.1, size=8)
+        params[i, 2] = rng.uniform(0.0, 2.0 * np.pi, size=8)
+    p = torch.from_numpy(params).to(device)
+    t = torch.arange(CHUNK_SAMPLES, device=device, dtype=torch.float64) / SAMPLE_RATE
+    out = torch.empty((chunks, CHUNK_SAMPLES), device=device, dtype=torch.float32)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed * 100003 + first_chunk)
+    for i in range(chunks):
+        x = (p[i, 1, :, None] * torch.sin(2.0 * np.pi * p[i, 0, :, None] * t[None, :]
+                                          + p[i, 2, :, None])).sum(0)
+        noise = torch.empty(CHUNK_SAMPLES, device=device, dtype=torch.float64)
+        noise.normal_(0.0, 0.01, generator=gen)
+        out[i] = (x + noise).clamp_(-1.0, 1.0).float()
+    return out
