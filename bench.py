@@ -49,6 +49,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-ops", action="store_true", help="skip the per-op roofline table")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--op", default=None,
+                   help="profiling mode: run only this op of the per-op table "
+                        "(warmup + steps launches, no flush) and print its timing")
     return p.parse_args()
 
 
@@ -187,7 +190,11 @@ def time_op(fn, iters: int, flush=None) -> float:
     return total / iters
 
 
-def op_table(peak: float) -> dict:
+def op_table(peak: float, only: str | None = None, iters_override: int | None = None) -> dict:
+    """Each op on its largest configuration; L2 flushed before every timed launch.
+
+    Each entry builds its inputs only when selected, so `only` (the --op
+    profiling mode) allocates and launches nothing else."""
     import torch
     import vlasr
     dev = torch.device("cuda")
@@ -201,78 +208,107 @@ def op_table(peak: float) -> dict:
         t.normal_(mean, std, generator=g)
         return t.to(dtype)
 
-    rows = {}
+    def add_layernorm():
+        x, r = rnd((8 * 1500, 1280)), rnd((8 * 1500, 1280))
+        gam, bet = rnd(1280, 1.0, 0.02), rnd(1280, 0.0, 0.02)
+        out = torch.empty_like(x)
+        return ("[8,1500,1280] bf16", 4 * x.numel() * 2,
+                lambda: vlasr.add_layernorm(r, x, gam, bet, out=out))
 
-    def add(name, config, nbytes, fn, iters=20, latency=False):
+    def gelu_erf():
+        gi = rnd((8 * 1500, 5120))
+        go = torch.empty_like(gi)
+        return "[8,1500,5120] bf16", 2 * gi.numel() * 2, lambda: vlasr.gelu_erf(gi, out=go)
+
+    def embed_gather():
+        table = rnd((151552, 2048), 0.0, 0.02)
+        ids = torch.randint(0, 151552, (4, 2048), device=dev, generator=g)
+        eo = torch.empty(4, 2048, 2048, dtype=bf, device=dev)
+        return ("ids [4,2048] from [151552,2048] bf16", 2 * eo.numel() * 2 + ids.numel() * 8,
+                lambda: vlasr.embed_gather(ids, table, out=eo))
+
+    def add_rmsnorm():
+        x, r, w = rnd((4 * 2048, 2048)), rnd((4 * 2048, 2048)), rnd(2048, 1.0, 0.02)
+        out = torch.empty_like(x)
+        return "[4,2048,2048] bf16", 4 * x.numel() * 2, lambda: vlasr.add_rmsnorm(r, x, w, out=out)
+
+    def swiglu():
+        gt, up = rnd((4 * 2048, 6144)), rnd((4 * 2048, 6144))
+        so = torch.empty_like(gt)
+        return "gate/up [4,2048,6144] bf16", 3 * gt.numel() * 2, lambda: vlasr.swiglu(gt, up, out=so)
+
+    def rope():
+        q, k = rnd((4, 2048, 16, 128)), rnd((4, 2048, 4, 128))
+        # algorithmic bytes: the rotated half of every head, read and written
+        return ("Q [4,2048,16,128] K [4,2048,4,128] rot 64", (q.numel() + k.numel()) * 2,
+                lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, seq_len=2048))
+
+    def _mel(chunks):
+        from vlasr.synth import audio_chunks_device
+        pcm = audio_chunks_device(chunks, 0, 7, dev)
+        mel = torch.empty(chunks, 128, 3000, device=dev)
+        ws = torch.empty(vlasr.logmel_workspace_bytes(chunks), dtype=torch.uint8, device=dev)
+        return (f"{chunks} x 30 s chunks", chunks * 3456000,
+                lambda: vlasr.logmel(pcm, out=mel, workspace=ws))
+
+    def decode_inputs():
+        q, k, v = rnd((64, 16, 128)), rnd((64, 4, 128)), rnd((64, 4, 128))
+        kc = torch.zeros(64 * 4096, 4, 128, dtype=bf, device=dev)
+        vc = torch.zeros_like(kc)
+        pos = torch.randint(0, 4096, (64,), device=dev, generator=g, dtype=torch.int64)
+        slots = torch.arange(64, device=dev) * 4096 + pos
+        return q, k, v, kc, vc, pos.to(torch.int32), slots
+
+    def decode_add_rmsnorm():
+        x, r, w = rnd((64, 2048)), rnd((64, 2048)), rnd(2048, 1.0, 0.02)
+        out = torch.empty_like(x)
+        return "[64,2048] bf16", 4 * x.numel() * 2, lambda: vlasr.add_rmsnorm(r, x, w, out=out)
+
+    def decode_rope():
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        return ("Q [64,16,128] K [64,4,128] rot 64", (q.numel() + k.numel()) * 2,
+                lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, positions=pos32))
+
+    def decode_kv_append():
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        return ("K/V [64,4,128] -> 64x4096 slots", 4 * k.numel() * 2,
+                lambda: vlasr.kv_append(k, v, kc, vc, slots))
+
+    def decode_rope_kv_append():
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        return ("fused RoPE + KV append", (q.numel() + 3 * k.numel()) * 2,
+                lambda: vlasr.rope_kv_append(q, k, v, kc, vc, pos32, slots, head_dim=128,
+                                             rotary_dim=64))
+
+    table = [  # name, builder, iterations, latency-bound
+        ("add_layernorm", add_layernorm, 20, False),
+        ("gelu_erf", gelu_erf, 20, False),
+        ("embed_gather", embed_gather, 20, False),
+        ("add_rmsnorm", add_rmsnorm, 20, False),
+        ("swiglu", swiglu, 20, False),
+        ("rope", rope, 20, False),
+        ("logmel", lambda: _mel(256), 5, False),
+        ("logmel_1chunk", lambda: _mel(1), 20, False),
+        ("decode_add_rmsnorm", decode_add_rmsnorm, 20, True),
+        ("decode_rope", decode_rope, 20, True),
+        ("decode_kv_append", decode_kv_append, 20, True),
+        ("decode_rope_kv_append", decode_rope_kv_append, 20, True),
+    ]
+    rows = {}
+    for name, build, iters, latency in table:
+        if only is not None and name != only:
+            continue
+        config, nbytes, fn = build()
         fn()
         torch.cuda.synchronize()
-        ms = time_op(fn, iters, flush)
+        ms = time_op(fn, iters_override or iters, flush)
         entry = {"config": config, "bytes": nbytes, "us": round(ms * 1e3, 2)}
         if not latency:
             gbs = nbytes / (ms * 1e-3) / 1e9
             entry.update({"gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 3)})
         rows[name] = entry
-
-    # config 1
-    x, r = rnd((8 * 1500, 1280)), rnd((8 * 1500, 1280))
-    gam, bet = rnd(1280, 1.0, 0.02), rnd(1280, 0.0, 0.02)
-    out = torch.empty_like(x)
-    add("add_layernorm", "[8,1500,1280] bf16", 4 * x.numel() * 2,
-        lambda: vlasr.add_layernorm(r, x, gam, bet, out=out))
-    del x, r, out
-    gi = rnd((8 * 1500, 5120))
-    go = torch.empty_like(gi)
-    add("gelu_erf", "[8,1500,5120] bf16", 2 * gi.numel() * 2, lambda: vlasr.gelu_erf(gi, out=go))
-    del gi, go
-    # config 2
-    table = rnd((151552, 2048), 0.0, 0.02)
-    ids = torch.randint(0, 151552, (4, 2048), device=dev, generator=g)
-    eo = torch.empty(4, 2048, 2048, dtype=bf, device=dev)
-    add("embed_gather", "ids [4,2048] from [151552,2048] bf16", 2 * eo.numel() * 2 + ids.numel() * 8,
-        lambda: vlasr.embed_gather(ids, table, out=eo))
-    del table, eo
-    x, r, w = rnd((4 * 2048, 2048)), rnd((4 * 2048, 2048)), rnd(2048, 1.0, 0.02)
-    out = torch.empty_like(x)
-    add("add_rmsnorm", "[4,2048,2048] bf16", 4 * x.numel() * 2,
-        lambda: vlasr.add_rmsnorm(r, x, w, out=out))
-    del x, r, out
-    gt, up = rnd((4 * 2048, 6144)), rnd((4 * 2048, 6144))
-    so = torch.empty_like(gt)
-    add("swiglu", "gate/up [4,2048,6144] bf16", 3 * gt.numel() * 2,
-        lambda: vlasr.swiglu(gt, up, out=so))
-    del gt, up, so
-    q, k = rnd((4, 2048, 16, 128)), rnd((4, 2048, 4, 128))
-    add("rope", "Q [4,2048,16,128] K [4,2048,4,128] rot 64", (q.numel() + k.numel()) * 2 // 2 * 2,
-        lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, seq_len=2048))
-    del q, k
-    # mel: one chunk (latency) and 256 chunks (throughput)
-    from vlasr.synth import audio_chunks_device
-    pcm = audio_chunks_device(256, 0, 7, dev)
-    mel = torch.empty(256, 128, 3000, device=dev)
-    ws = torch.empty(vlasr.logmel_workspace_bytes(256), dtype=torch.uint8, device=dev)
-    add("logmel", "256 x 30 s chunks", 256 * 3456000,
-        lambda: vlasr.logmel(pcm, out=mel, workspace=ws), iters=5)
-    add("logmel_1chunk", "1 x 30 s chunk", 3456000,
-        lambda: vlasr.logmel(pcm[:1], out=mel[:1], workspace=ws), iters=20)
-    del pcm, mel
-    # config 3: decode step (latency-bound)
-    x, r, w = rnd((64, 2048)), rnd((64, 2048)), rnd(2048, 1.0, 0.02)
-    out = torch.empty_like(x)
-    add("decode_add_rmsnorm", "[64,2048] bf16", 4 * x.numel() * 2,
-        lambda: vlasr.add_rmsnorm(r, x, w, out=out), latency=True)
-    q, k, v = rnd((64, 16, 128)), rnd((64, 4, 128)), rnd((64, 4, 128))
-    kc = torch.zeros(64 * 4096, 4, 128, dtype=bf, device=dev)
-    vc = torch.zeros_like(kc)
-    pos = torch.randint(0, 4096, (64,), device=dev, generator=g, dtype=torch.int64)
-    slots = torch.arange(64, device=dev) * 4096 + pos
-    pos32 = pos.to(torch.int32)
-    add("decode_rope", "Q [64,16,128] K [64,4,128] rot 64", (q.numel() + k.numel()) * 2,
-        lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, positions=pos32), latency=True)
-    add("decode_kv_append", "K/V [64,4,128] -> 64x4096 slots", 4 * k.numel() * 2,
-        lambda: vlasr.kv_append(k, v, kc, vc, slots), latency=True)
-    add("decode_rope_kv_append", "fused RoPE + KV append", (q.numel() + 3 * k.numel()) * 2,
-        lambda: vlasr.rope_kv_append(q, k, v, kc, vc, pos32, slots, head_dim=128, rotary_dim=64),
-        latency=True)
+        del fn
+        torch.cuda.empty_cache()
     del flush_buf
     torch.cuda.empty_cache()
     return rows
@@ -341,6 +377,15 @@ def main() -> None:
         return
     import torch
     import vlasr
+    if args.op is not None:
+        torch.cuda.set_device(0)
+        vlasr.load()
+        peak, _ = peaks()
+        rows = op_table(peak, only=args.op, iters_override=args.steps)
+        if not rows:
+            raise SystemExit(f"unknown op {args.op}")
+        print(json.dumps({"op": args.op, **rows[args.op]}), flush=True)
+        return
     from vlasr.pipeline import ChainShape, EncoderNormChain, shard_range
     from vlasr.synth import audio_chunks_device
 
