@@ -113,6 +113,35 @@ VL_EXPORT size_t vl_logmel_workspace_bytes(int64_t chunks);
 VL_EXPORT int vl_logmel(const float* pcm, int64_t chunks, float* out, void* workspace,
               size_t workspace_bytes, void* stream);
 
+/* Largest chunk count vl_logmel_noalloc accepts in one call. */
+#define VL_LOGMEL_NOALLOC_MAX_CHUNKS 1024
+
+/*
+ * vl_logmel for callers that cannot allocate device memory.  This entry
+ * point has no counterpart in the reference.
+ *
+ * Some hosts cannot call cudaMalloc or hand this library a scratch buffer:
+ * a process whose GPU memory is all reserved up front by a fixed budget or
+ * arena (a serving process, or an engine sharing the GPU under a VRAM cap as
+ * the reference's native engine does), a plugin running inside another
+ * framework's callback where allocating is not allowed, or a latency-
+ * critical path that must never wait on the allocator.  Such callers pass
+ * only pcm and out (the same layouts as vl_logmel); the per-tile maxima the
+ * kernel needs live in one fixed array inside the library, sized for
+ * VL_LOGMEL_NOALLOC_MAX_CHUNKS chunks (512,000 bytes, held on every GPU that
+ * loads the library until the process exits).  chunks above that limit
+ * return VL_ERR_INVALID.  Nothing is allocated, freed or synchronised.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and raises the kernel's shared-memory limit; make
+ * that first call before any stream capture.  Every call shares the one
+ * array and it keeps whatever the previous call left there; nothing in it
+ * has to start at zero because each call writes every slot before reading
+ * it.  Calls that can overlap on the GPU (several streams, or several host
+ * threads on one device) race on the array: serialise them.
+ */
+VL_EXPORT int vl_logmel_noalloc(const float* pcm, int64_t chunks, float* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Norms                                                                     */
 /* ------------------------------------------------------------------------ */

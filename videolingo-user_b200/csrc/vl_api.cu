@@ -114,6 +114,24 @@ int vl_logmel(const float* pcm, int64_t chunks, float* out, void* workspace,
                      "vl_logmel");
 }
 
+int vl_logmel_noalloc(const float* pcm, int64_t chunks, float* out, void* stream) {
+  if (pcm == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_logmel_noalloc: null pointer (pcm=%p out=%p)", pcm, out);
+  if (chunks <= 0 || chunks > VL_LOGMEL_NOALLOC_MAX_CHUNKS)
+    return fail(VL_ERR_INVALID,
+                "vl_logmel_noalloc: chunks must be in [1, %d] (the size of its fixed scratch "
+                "array), got %lld; use vl_logmel with a workspace for more",
+                VL_LOGMEL_NOALLOC_MAX_CHUNKS, static_cast<long long>(chunks));
+  if (!vl::aligned16(pcm) || !vl::aligned16(out))
+    return fail(VL_ERR_INVALID, "vl_logmel_noalloc: pcm and out must be 16-byte aligned");
+  const int64_t in_bytes = chunks * VL_MEL_CHUNK_SAMPLES * 4;
+  const int64_t out_bytes = chunks * VL_MEL_BINS * VL_MEL_FRAMES * 4;
+  if (overlaps(pcm, in_bytes, out, out_bytes))
+    return fail(VL_ERR_INVALID, "vl_logmel_noalloc: pcm and out must not overlap");
+  return exec_status(vl::launch_logmel_noalloc(pcm, chunks, out, static_cast<cudaStream_t>(stream)),
+                     "vl_logmel_noalloc");
+}
+
 static int check_norm(const char* op, void* residual, const void* delta, const void* weight,
                       void* out, int64_t rows, int64_t cols, float eps, int dtype) {
   if (residual == nullptr || weight == nullptr || out == nullptr)

@@ -61,5 +61,8 @@ cudaError_t launch_kv_append(const void* k, const void* v, void* k_cache, void* 
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream);
+// Same, with the library's fixed scratch array instead of a caller workspace.
+cudaError_t launch_logmel_noalloc(const float* pcm, int64_t chunks, float* out,
+                                  cudaStream_t stream);
 
 }  // namespace vl

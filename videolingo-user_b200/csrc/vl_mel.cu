@@ -20,6 +20,7 @@
 // log-mel (1.5 MB per chunk) stays resident in the 126 MB L2 between the two
 // kernels, so HBM sees the PCM once and the features once.
 #include <atomic>
+#include <mutex>
 
 #include "vl_common.cuh"
 #include "vl_kernels.h"
@@ -263,7 +264,34 @@ cudaError_t enable_large_smem(size_t smem) {
   return err;
 }
 
+// Scratch of vl_logmel_noalloc: the per-tile maxima of up to
+// VL_LOGMEL_NOALLOC_MAX_CHUNKS chunks (512,000 bytes), a fixed array inside
+// the library so that entry point allocates nothing.  Host code must not
+// use the symbol itself as a pointer (it names a host-side shadow); it
+// fetches the device address once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) float g_noalloc_tile_max[VL_LOGMEL_NOALLOC_MAX_CHUNKS * kTilesPerChunk];
+
 }  // namespace
+
+// Device address of g_noalloc_tile_max on the current device, looked up on
+// the first call per device (that device current) and cached.
+cudaError_t noalloc_tile_max(float** ptr) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_tile_max);
+    if (err != cudaSuccess) return err;
+    addr[dev] = static_cast<float*>(p);
+  }
+  *ptr = addr[dev];
+  return cudaSuccess;
+}
 
 size_t logmel_workspace_bytes(int64_t chunks) {
   const size_t raw = static_cast<size_t>(chunks) * kTilesPerChunk * sizeof(float);
@@ -288,6 +316,18 @@ cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* t
     if (err != cudaSuccess) return err;
   }
   return cudaSuccess;
+}
+
+}  // namespace vl
+
+namespace vl {
+
+cudaError_t launch_logmel_noalloc(const float* pcm, int64_t chunks, float* out,
+                                  cudaStream_t stream) {
+  float* tile_max = nullptr;
+  const cudaError_t err = noalloc_tile_max(&tile_max);
+  if (err != cudaSuccess) return err;
+  return launch_logmel(pcm, chunks, out, tile_max, stream);
 }
 
 }  // namespace vl
