@@ -178,3 +178,37 @@ def test_swiglu_full_config(dev):
     out = vlasr.swiglu(from_np(g, torch.bfloat16, dev), from_np(u, torch.bfloat16, dev))
     exp = oracle.swiglu(g, u, "bf16")
     assert normwise(to_np(out), exp) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_gelu_table_path_is_bit_exact_over_all_inputs(dev, dtype):
+    """Every 16-bit pattern (NaN/Inf/subnormals included): the table path
+    (>= 1M elements) equals the direct erff evaluation (small inputs) bit for
+    bit, and the finite results match the oracle."""
+    td = torch_dtype(dtype)
+    patterns = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(td).to(dev)
+    direct = vlasr.gelu_erf(patterns)                  # 65536 elements: direct path
+    table = vlasr.gelu_erf(patterns.repeat(32))        # 2,097,152 elements: table path
+    torch.cuda.synchronize()
+    assert torch.equal(table.view(torch.int16), direct.repeat(32).view(torch.int16))
+    x = to_np(patterns)
+    finite = np.isfinite(x)
+    exp = oracle.gelu(x[finite].reshape(1, -1), None, dtype)[0]
+    got = to_np(direct)[finite]
+    assert normwise(got, exp) <= TOL[dtype]
+    assert (got == exp).mean() > 0.999
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_gelu_bias_table_path_matches_direct_path(dev, dtype):
+    rng = np.random.default_rng(77)
+    rows, cols = 512, 4096                              # 2M elements: table path
+    x = oracle.round_to(rng.normal(0, 3, (rows, cols)), dtype)
+    b = oracle.round_to(rng.normal(0, 1, cols), dtype)
+    td = torch_dtype(dtype)
+    xt, bt = from_np(x, td, dev), from_np(b, td, dev)
+    table = vlasr.gelu_erf(xt, bt)
+    pieces = [vlasr.gelu_erf(xt[r:r + 128], bt) for r in range(0, rows, 128)]  # direct path
+    torch.cuda.synchronize()
+    assert torch.equal(table.view(torch.int16), torch.cat(pieces).view(torch.int16))
+    assert normwise(to_np(table), oracle.gelu(x, b, dtype)) <= TOL[dtype]

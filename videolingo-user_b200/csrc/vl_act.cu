@@ -7,6 +7,17 @@
 //   silu_mul_kernel (decoder.cu:103-109) g = half(g / (1 + __expf(-g)) * u)
 // Both are pure streams: 16-byte vector loads, several vectors in flight per
 // thread, grid sized to a whole number of waves over the SMs.
+//
+// GELU for 16-bit storage types runs as a table lookup: an input is one of
+// 65536 bit patterns, so the library builds, once per device, a 128 KB table
+// per type holding round(gelu(x)) for every pattern - computed on the device
+// with the very expression above, so the result is bit-identical to
+// evaluating erff per element - and each block stages the table in shared
+// memory.  That replaces ~29 instructions per element (erff plus conversions
+// saturate the special-function pipe) by ~3, leaving the kernel HBM-bound.
+#include <mutex>
+#include <type_traits>
+
 #include "vl_common.cuh"
 #include "vl_kernels.h"
 
@@ -159,6 +170,173 @@ __global__ void swiglu_scalar_kernel(const T* gate, const T* up, T* out, int64_t
   }
 }
 
+// ---------------------------------------------------------------------------
+// Table GELU (bf16 / fp16)
+// ---------------------------------------------------------------------------
+constexpr int kLutThreads = 1024;          // one block per SM (the table fills 128 KB of smem)
+constexpr int kLutEntries = 65536;
+constexpr int kLutBytes = kLutEntries * 2;
+constexpr int64_t kLutMinElems = 1 << 20;  // below this the table load does not pay off
+
+// [0]: bf16 bits -> bf16 bits of round(gelu(x)); [1]: the same for fp16.
+static __device__ __align__(16) uint16_t g_gelu_lut[2][kLutEntries];
+
+template <typename T>
+struct LutSlot;
+template <>
+struct LutSlot<__nv_bfloat16> {
+  static constexpr int kIndex = 0;
+};
+template <>
+struct LutSlot<__half> {
+  static constexpr int kIndex = 1;
+};
+
+__global__ void gelu_lut_init_kernel(uint16_t* lut) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kLutEntries) return;
+  // Same conversion and packing instructions as the direct kernels.
+  const float xb = bf16_lo(static_cast<uint32_t>(i));
+  lut[i] = static_cast<uint16_t>(pack_bf16x2(gelu_erf(xb), 0.f) & 0xffffu);
+  const float xh = __half2float(__ushort_as_half(static_cast<unsigned short>(i)));
+  lut[kLutEntries + i] = static_cast<uint16_t>(pack_f16x2(gelu_erf(xh), 0.f) & 0xffffu);
+}
+
+template <typename T, bool kBias>
+__global__ void __launch_bounds__(kLutThreads, 1)
+    gelu_lut_kernel(const T* in, const T* __restrict__ bias, T* out, int64_t nvec,
+                    uint32_t vec_per_row, const uint16_t* __restrict__ lut_global) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  extern __shared__ __align__(16) unsigned char lut_raw[];
+  {
+    uint4* dst = reinterpret_cast<uint4*>(lut_raw);
+    const uint4* src = reinterpret_cast<const uint4*>(lut_global);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < kLutBytes / 16; i += kLutThreads) dst[i] = __ldg(src + i);
+  }
+  __syncthreads();
+  const uint16_t* lut = reinterpret_cast<const uint16_t*>(lut_raw);
+  const uint4* src = reinterpret_cast<const uint4*>(in);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  const uint4* bvec = reinterpret_cast<const uint4*>(bias);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kLutThreads;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kLutThreads + threadIdx.x; base < nvec;
+       base += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < nvec) v[u] = ld_stream(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < nvec) {
+        uint4 w = v[u];
+        if (kBias) {
+          float x[E], b[E];
+          S::unpack(w, x);
+          S::unpack(__ldg(bvec + static_cast<uint32_t>(i) % vec_per_row), b);
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] = x[e] + b[e];
+          w = S::pack(x);  // round(x + b), as the reference stores it before GELU
+        }
+        uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t lo = lut[words[j] & 0xffffu];
+          const uint32_t hi = lut[words[j] >> 16];
+          words[j] = lo | (hi << 16);
+        }
+        st_stream(dst + i, make_uint4(words[0], words[1], words[2], words[3]));
+      }
+    }
+  }
+}
+
+struct LutState {
+  std::mutex mu;
+  int state = 0;  // 0 = not built, 1 = ready, 2 = unavailable
+  uint16_t* ptr = nullptr;
+};
+LutState g_lut_state[64];
+
+// Device address of the GELU tables on the current device, building them on
+// first use: a private stream runs the init kernel and is synchronised once,
+// so every later launch on any stream sees a complete table.  Returns null -
+// and the caller evaluates erff directly, with identical results - while the
+// caller's stream is being captured before the table exists, or if building
+// it failed.
+const uint16_t* gelu_table(cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  LutState& st = g_lut_state[dev];
+  std::lock_guard<std::mutex> lock(st.mu);
+  if (st.state == 1) return st.ptr;
+  if (st.state == 2) return nullptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  void* p = nullptr;
+  cudaStream_t s = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&p, g_gelu_lut);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(gelu_lut_kernel<__nv_bfloat16, false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(gelu_lut_kernel<__nv_bfloat16, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(gelu_lut_kernel<__half, false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(gelu_lut_kernel<__half, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes);
+  if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (err == cudaSuccess) {
+    gelu_lut_init_kernel<<<kLutEntries / 256, 256, 0, s>>>(static_cast<uint16_t*>(p));
+    err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  }
+  if (s != nullptr) cudaStreamDestroy(s);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    st.state = 2;
+    return nullptr;
+  }
+  st.ptr = static_cast<uint16_t*>(p);
+  st.state = 1;
+  return st.ptr;
+}
+
+template <typename T>
+bool gelu_via_table(const void* in, const void* bias, void* out, int64_t rows, int64_t cols,
+                    cudaStream_t stream) {
+  constexpr int E = Storage<T>::kVec;
+  const int64_t n = rows * cols;
+  if (n < kLutMinElems || n % E != 0 || !aligned16(in) || !aligned16(out)) return false;
+  if (bias != nullptr && (!aligned16(bias) || cols % E != 0 || n / E >= (int64_t(1) << 32)))
+    return false;
+  const uint16_t* table = gelu_table(stream);
+  if (table == nullptr) return false;
+  table += LutSlot<T>::kIndex * kLutEntries;
+  const int64_t nvec = n / E;
+  int64_t blocks = (nvec + int64_t(kLutThreads) * kUnroll - 1) / (int64_t(kLutThreads) * kUnroll);
+  if (blocks > sm_count()) blocks = sm_count();
+  const uint32_t vpr = bias ? static_cast<uint32_t>(cols / E) : 1u;
+  if (bias)
+    gelu_lut_kernel<T, true><<<static_cast<unsigned>(blocks), kLutThreads, kLutBytes, stream>>>(
+        static_cast<const T*>(in), static_cast<const T*>(bias), static_cast<T*>(out), nvec, vpr,
+        table);
+  else
+    gelu_lut_kernel<T, false><<<static_cast<unsigned>(blocks), kLutThreads, kLutBytes, stream>>>(
+        static_cast<const T*>(in), nullptr, static_cast<T*>(out), nvec, vpr, table);
+  return true;
+}
+
 unsigned flat_blocks(int64_t nvec) {
   const int64_t per_block = static_cast<int64_t>(kActThreads) * kUnroll;
   const int64_t need = (nvec + per_block - 1) / per_block;
@@ -181,6 +359,9 @@ cudaError_t gelu_typed(const void* in, const void* bias, void* out, int64_t rows
   constexpr int E = Storage<T>::kVec;
   const T* x = static_cast<const T*>(in);
   T* y = static_cast<T*>(out);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (gelu_via_table<T>(in, bias, out, rows, cols, stream)) return cudaGetLastError();
+  }
   const bool vec_ok = aligned16(in) && aligned16(out) && (bias == nullptr || aligned16(bias));
   if (bias == nullptr && vec_ok && ((rows * cols) % E == 0)) {
     const int64_t nvec = rows * cols / E;
