@@ -471,7 +471,7 @@ def main() -> None:
         mel_host = torch.empty((shape.chunks, 128, 3000), dtype=torch.float32).pin_memory()
         y_host = torch.empty((shape.rows, shape.hidden), dtype=torch.bfloat16).pin_memory()
         pcm_dev = torch.empty_like(pcm)
-        groups = max(1, min(8, shape.chunks // 8))
+        groups = max(1, min(16, shape.chunks // 8))
         for _ in range(max(1, args.warmup)):
             chain.step_host(pcm_host, mel_host, y_host, pcm_dev, groups=groups)
         torch.cuda.synchronize()

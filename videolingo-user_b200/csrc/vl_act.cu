@@ -174,6 +174,7 @@ __global__ void swiglu_scalar_kernel(const T* gate, const T* up, T* out, int64_t
 // Table GELU (bf16 / fp16)
 // ---------------------------------------------------------------------------
 constexpr int kLutThreads = 1024;          // one block per SM (the table fills 128 KB of smem)
+constexpr int kLutUnroll = 8;              // 16-byte vectors in flight per thread (128 KB per SM)
 constexpr int kLutEntries = 65536;
 constexpr int kLutBytes = kLutEntries * 2;
 constexpr int64_t kLutMinElems = 1 << 20;  // below this the table load does not pay off
@@ -222,15 +223,15 @@ __global__ void __launch_bounds__(kLutThreads, 1)
   const uint4* bvec = reinterpret_cast<const uint4*>(bias);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kLutThreads;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * kLutThreads + threadIdx.x; base < nvec;
-       base += stride * kUnroll) {
-    uint4 v[kUnroll];
+       base += stride * kLutUnroll) {
+    uint4 v[kLutUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kLutUnroll; ++u) {
       const int64_t i = base + u * stride;
       if (i < nvec) v[u] = ld_stream(src + i);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kLutUnroll; ++u) {
       const int64_t i = base + u * stride;
       if (i < nvec) {
         uint4 w = v[u];
@@ -324,7 +325,8 @@ bool gelu_via_table(const void* in, const void* bias, void* out, int64_t rows, i
   if (table == nullptr) return false;
   table += LutSlot<T>::kIndex * kLutEntries;
   const int64_t nvec = n / E;
-  int64_t blocks = (nvec + int64_t(kLutThreads) * kUnroll - 1) / (int64_t(kLutThreads) * kUnroll);
+  int64_t blocks =
+      (nvec + int64_t(kLutThreads) * kLutUnroll - 1) / (int64_t(kLutThreads) * kLutUnroll);
   if (blocks > sm_count()) blocks = sm_count();
   const uint32_t vpr = bias ? static_cast<uint32_t>(cols / E) : 1u;
   if (bias)
