@@ -200,8 +200,11 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
     dev = torch.device("cuda")
     bf = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(1234)
-    flush_buf = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    flush = lambda: flush_buf.fill_(1)  # noqa: E731  (larger than the 126 MB L2)
+    # L2 flush by READING 512 MB (4x the 126 MB L2): it evicts the op's
+    # inputs and leaves L2 clean, so the timed launch does not also pay for
+    # writing back a flush buffer's dirty lines.
+    flush_buf = torch.ones(128 * 1024 * 1024, dtype=torch.int32, device=dev)
+    flush = lambda: flush_buf.max()  # noqa: E731
 
     def rnd(shape, mean=0.0, std=1.0, dtype=bf):
         t = torch.empty(shape, device=dev, dtype=torch.float32)

@@ -339,10 +339,12 @@ bool gelu_via_table(const void* in, const void* bias, void* out, int64_t rows, i
   return true;
 }
 
-unsigned flat_blocks(int64_t nvec) {
+// Grid of a grid-stride stream kernel: enough blocks for the data, at most
+// the number resident at once (a single persistent wave, no tail wave).
+unsigned flat_blocks(const void* kernel, int64_t nvec) {
   const int64_t per_block = static_cast<int64_t>(kActThreads) * kUnroll;
   const int64_t need = (nvec + per_block - 1) / per_block;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 x 256 threads resident per SM
+  const int64_t cap = resident_blocks(kernel, kActThreads, 0);
   return static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
 }
 
@@ -367,7 +369,8 @@ cudaError_t gelu_typed(const void* in, const void* bias, void* out, int64_t rows
   const bool vec_ok = aligned16(in) && aligned16(out) && (bias == nullptr || aligned16(bias));
   if (bias == nullptr && vec_ok && ((rows * cols) % E == 0)) {
     const int64_t nvec = rows * cols / E;
-    gelu_flat_kernel<T><<<flat_blocks(nvec), kActThreads, 0, stream>>>(x, y, nvec);
+    gelu_flat_kernel<T><<<flat_blocks(reinterpret_cast<const void*>(gelu_flat_kernel<T>), nvec),
+                           kActThreads, 0, stream>>>(x, y, nvec);
   } else if (bias != nullptr && vec_ok && cols % E == 0 && cols / E < (1 << 30)) {
     const int vpr = static_cast<int>(cols / E);
     gelu_bias_kernel<T><<<row_grid(vpr, rows), kActThreads, 0, stream>>>(
@@ -394,7 +397,8 @@ cudaError_t swiglu_typed(const void* gate, const void* up, void* out, int64_t ro
                       gs % E == 0 && us % E == 0 && os % E == 0;
   if (vec_ok && gs == cols && us == cols && os == cols) {
     const int64_t nvec = rows * cols / E;
-    swiglu_flat_kernel<T><<<flat_blocks(nvec), kActThreads, 0, stream>>>(g, u, o, nvec);
+    swiglu_flat_kernel<T><<<flat_blocks(reinterpret_cast<const void*>(swiglu_flat_kernel<T>), nvec),
+                             kActThreads, 0, stream>>>(g, u, o, nvec);
   } else if (vec_ok && cols / E < (1 << 30)) {
     const int vpr = static_cast<int>(cols / E);
     swiglu_rows_kernel<T><<<row_grid(vpr, rows), kActThreads, 0, stream>>>(g, u, o, rows, vpr, gs,

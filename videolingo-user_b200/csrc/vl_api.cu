@@ -9,7 +9,9 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "vl_common.cuh"
 #include "vl_kernels.h"
@@ -66,6 +68,29 @@ int sm_count() {
     v = 148;
   cache[dev].store(v, std::memory_order_relaxed);
   return v;
+}
+
+int resident_blocks(const void* kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return sm_count();
+  const auto key = std::make_tuple(dev, kernel, threads, smem);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  const int blocks = per_sm * sm_count();
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = blocks;
+  return blocks;
 }
 
 }  // namespace vl

@@ -142,4 +142,9 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device id).
 int sm_count();
 
+// Blocks of `kernel` (at `threads` threads and `smem` dynamic shared bytes)
+// that are resident on the whole current device at once: the grid size of a
+// persistent, grid-stride launch.  Cached per (device, kernel).
+int resident_blocks(const void* kernel, int threads, size_t smem);
+
 }  // namespace vl

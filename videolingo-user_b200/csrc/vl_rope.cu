@@ -37,16 +37,54 @@ __device__ __forceinline__ int64_t token_position(const RopeArgs& a, int64_t r) 
   return a.pos_offset + static_cast<int64_t>(a.positions[src * a.positions_stride]);
 }
 
+// Head row of task i of this block: task = (token t, head h, vector/pair j).
+template <typename T>
+__device__ __forceinline__ T* task_head(const RopeArgs& a, int64_t t0, int i, int tasks,
+                                        int per_head, int* t_out, int* j_out) {
+  const int t = i / tasks;
+  const int rem = i - t * tasks;
+  const int h = rem / per_head;
+  *t_out = t;
+  *j_out = rem - h * per_head;
+  const int64_t r = t0 + t;
+  return h < a.n_q_heads
+             ? static_cast<T*>(a.q) + r * a.q_row_stride + static_cast<int64_t>(h) * a.head_dim
+             : static_cast<T*>(a.k) + r * a.k_row_stride +
+                   static_cast<int64_t>(h - a.n_q_heads) * a.head_dim;
+}
+
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(kRopeThreads)
-    rope_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq, int tokens_per_block) {
+    rope_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq,
+                int tokens_per_block) {
   using S = Storage<T>;
   constexpr int E = S::kVec;
+  constexpr int G = 4;  // tasks whose vectors are in flight per thread
   extern __shared__ float2 cs[];  // [tokens_per_block][half_rot] (cos, sin)
   const int half_rot = a.rotary_dim / 2;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tokens_per_block;
   int nt = tokens_per_block;
   if (t0 + nt > a.tokens) nt = static_cast<int>(a.tokens - t0);
+  const int heads = a.n_q_heads + a.n_k_heads;
+  const int per_head = kVec ? half_rot / E : half_rot;
+  const int tasks = heads * per_head;
+  const int ntask = nt * tasks;
+
+  // Vector path: the first group of x1/x2 vectors is requested before the
+  // fp64 cos/sin evaluation, so the HBM latency overlaps it.
+  uint4 x1v[G], x2v[G];
+  if (kVec) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int i = threadIdx.x + g * kRopeThreads;
+      if (i < ntask) {
+        int t, j;
+        T* head = task_head<T>(a, t0, i, tasks, per_head, &t, &j);
+        x1v[g] = ld_vec(head + j * E);
+        x2v[g] = ld_vec(head + half_rot + j * E);
+      }
+    }
+  }
 
   for (int i = threadIdx.x; i < nt * half_rot; i += kRopeThreads) {
     const int t = i / half_rot, d = i % half_rot;
@@ -57,35 +95,46 @@ __global__ void __launch_bounds__(kRopeThreads)
   }
   __syncthreads();
 
-  const int heads = a.n_q_heads + a.n_k_heads;
-  const int per_head = kVec ? half_rot / E : half_rot;
-  const int tasks = heads * per_head;
-  for (int i = threadIdx.x; i < nt * tasks; i += kRopeThreads) {
-    const int t = i / tasks;
-    const int rem = i % tasks;
-    const int h = rem / per_head, j = rem % per_head;
-    const int64_t r = t0 + t;
-    T* head = h < a.n_q_heads
-                  ? static_cast<T*>(a.q) + r * a.q_row_stride + static_cast<int64_t>(h) * a.head_dim
-                  : static_cast<T*>(a.k) + r * a.k_row_stride +
-                        static_cast<int64_t>(h - a.n_q_heads) * a.head_dim;
-    const float2* cst = cs + t * half_rot;
-    if (kVec) {
-      uint4* p1 = reinterpret_cast<uint4*>(head + j * E);
-      uint4* p2 = reinterpret_cast<uint4*>(head + half_rot + j * E);
-      float x1[E], x2[E], y1[E], y2[E];
-      S::unpack(ld_vec(p1), x1);
-      S::unpack(ld_vec(p2), x2);
+  if (kVec) {
+    for (int base = threadIdx.x; base < ntask; base += kRopeThreads * G) {
+      if (base != static_cast<int>(threadIdx.x)) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float c = cst[j * E + e].x, s = cst[j * E + e].y;
-        y1[e] = x1[e] * c - x2[e] * s;
-        y2[e] = x2[e] * c + x1[e] * s;
+        for (int g = 0; g < G; ++g) {
+          const int i = base + g * kRopeThreads;
+          if (i < ntask) {
+            int t, j;
+            T* head = task_head<T>(a, t0, i, tasks, per_head, &t, &j);
+            x1v[g] = ld_vec(head + j * E);
+            x2v[g] = ld_vec(head + half_rot + j * E);
+          }
+        }
       }
-      st_vec(p1, S::pack(y1));
-      st_vec(p2, S::pack(y2));
-    } else {
-      const float c = cst[j].x, s = cst[j].y;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int i = base + g * kRopeThreads;
+        if (i < ntask) {
+          int t, j;
+          T* head = task_head<T>(a, t0, i, tasks, per_head, &t, &j);
+          const float2* cst = cs + t * half_rot + j * E;
+          float x1[E], x2[E], y1[E], y2[E];
+          S::unpack(x1v[g], x1);
+          S::unpack(x2v[g], x2);
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float c = cst[e].x, s = cst[e].y;
+            y1[e] = x1[e] * c - x2[e] * s;
+            y2[e] = x2[e] * c + x1[e] * s;
+          }
+          st_vec(head + j * E, S::pack(y1));
+          st_vec(head + half_rot + j * E, S::pack(y2));
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < ntask; i += kRopeThreads) {
+      int t, j;
+      T* head = task_head<T>(a, t0, i, tasks, per_head, &t, &j);
+      const float c = cs[t * half_rot + j].x, s = cs[t * half_rot + j].y;
       const float x1 = S::to_float(head[j]);
       const float x2 = S::to_float(head[j + half_rot]);
       head[j] = S::from_float(x1 * c - x2 * s);
@@ -137,8 +186,8 @@ cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
   if (a.v != nullptr)
     vec = vec && aligned16(a.v) && aligned16(a.k_cache) && aligned16(a.v_cache) &&
           row_elems % E == 0;
-  // Enough blocks to cover the SMs several times, up to 8 tokens per block.
-  const int64_t want_blocks = static_cast<int64_t>(sm_count()) * 4;
+  // Enough blocks to fill every SM's 16 resident blocks, up to 8 tokens each.
+  const int64_t want_blocks = static_cast<int64_t>(sm_count()) * 16;
   int64_t tpb = (a.tokens + want_blocks - 1) / want_blocks;
   if (tpb < 1) tpb = 1;
   if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;

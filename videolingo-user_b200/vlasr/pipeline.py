@@ -57,6 +57,18 @@ class ChainShape:
                 "total": mel + self.layers * (ln + gelu)}
 
 
+def gather_outputs(full: torch.Tensor, shard: torch.Tensor, group=None) -> None:
+    """All-gather every rank's encoder-norm rows into `full` in global chunk
+    order (rank r's contiguous chunk range lands at its offset).  Requires
+    equal shards, i.e. world size dividing the chunk count, as the
+    benchmark's 256 chunks over 1/2/4/8 ranks do."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if full.shape[0] != shard.shape[0] * world or full.shape[1:] != shard.shape[1:]:
+        raise ValueError("gather_outputs needs equal shards: full rows = world * shard rows")
+    dist.all_gather_into_tensor(full, shard.contiguous(), group=group)
+
+
 def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous chunk range [begin, end) of `rank`; equal shares when world divides total."""
     base, extra = divmod(total, world)
@@ -124,8 +136,7 @@ class EncoderNormChain:
 
     def all_gather(self) -> None:
         if self.y_all is not None:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.y_all, self.y, group=self.group)
+            gather_outputs(self.y_all, self.y, self.group)
 
     def step(self, pcm: torch.Tensor, timer=None) -> None:
         """One pass over this rank's chunks with device-resident PCM.
