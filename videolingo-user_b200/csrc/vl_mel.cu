@@ -13,12 +13,15 @@
 //     400 = 20 x 20: stage 1 = 20 DFT-20s over stride-20 samples + W400
 //     twiddles, stage 2 = 20 DFT-20s (each DFT-20 = 4 x 5 in registers)
 //   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry
-//   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense)
+//   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense),
+//     one task per (frame, run of mel bins) with runs of equal cost
 //   log10(max(., 1e-10)) -> out, tile max -> workspace
-// and a second, light kernel folds the tile maxima of each chunk and applies
-// max(x, max-8) then (x+4)/4 in place.  Chunks are processed in batches whose
-// log-mel (1.5 MB per chunk) stays resident in the 126 MB L2 between the two
-// kernels, so HBM sees the PCM once and the features once.
+// The three stage buffers (samples, stage-1 transpose, packed spectrum)
+// share one 40 KB region, so three tiles fit on an SM.  A second, light
+// kernel folds the tile maxima of each chunk and applies max(x, max-8) then
+// (x+4)/4 in place.  Chunks are processed in batches whose log-mel (1.5 MB
+// per chunk) stays resident in the 126 MB L2 between the two kernels, so
+// HBM sees the PCM once and the features once.
 #include <atomic>
 #include <mutex>
 
@@ -45,17 +48,20 @@ constexpr int kNormSlices = 16;            // normalise blocks per chunk
 constexpr int kBatchChunks = 32;           // chunks per L2-resident batch
 
 struct MelSmem {
-  float samples[kTileSamples];
-  float window[400];
-  float2 tw[400];
-  float2 z[kPairs][400];                   // packed spectra Z[p][k]
+  // samples -> stage-1 output t[p][k1][n2] -> packed spectra z[p][k]; each
+  // stage reads its input into registers and passes a barrier before writing.
   union {
-    float2 t[kPairs][20][kTRow];           // stage-1 output, transposed
-    float p[kTileFrames][kBins];           // power spectra
+    float samples[kTileSamples];
+    float2 t[kPairs][20][kTRow];
+    float2 z[kPairs][400];
   } u;
+  float p[kTileFrames][kBins];             // power spectra
+  float window[400];
+  float2 tw[362];                          // W400^m, m <= 19 * 19
   float melw[VL_MEL_NNZ];
   int mel_off[kMel + 1];
   int mel_lo[kMel];
+  int group[VL_MEL_GROUPS + 1];
   float red[kThreads / 32];
 };
 
@@ -114,7 +120,7 @@ __device__ __forceinline__ int reflect(int j) {
   return j;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     mel_tile_kernel(const float* __restrict__ pcm, float* __restrict__ out,
                     float* __restrict__ tile_max, int chunk0) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -125,86 +131,94 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int f0 = tile * kTileFrames;
   const float* src = pcm + chunk * kChunkSamples;
   const int j0 = f0 * kHop - kPad;
+  const bool fft_thread = tid < kPairs * 20;
 
   // ---- stage 0: samples, window, twiddles and filterbank into shared memory
   if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
     const float4* s4 = reinterpret_cast<const float4*>(src + j0);
-    float4* d4 = reinterpret_cast<float4*>(sm.samples);
+    float4* d4 = reinterpret_cast<float4*>(sm.u.samples);
     for (int i = tid; i < kTileSamples / 4; i += kThreads) d4[i] = __ldcs(s4 + i);
   } else {
-    for (int i = tid; i < kTileSamples; i += kThreads) sm.samples[i] = src[reflect(j0 + i)];
+    for (int i = tid; i < kTileSamples; i += kThreads) sm.u.samples[i] = src[reflect(j0 + i)];
   }
-  for (int i = tid; i < 400; i += kThreads) {
-    sm.window[i] = mel::kWindow[i];
-    sm.tw[i] = mel::kTwiddle400[i];
-  }
+  for (int i = tid; i < 400; i += kThreads) sm.window[i] = mel::kWindow[i];
+  for (int i = tid; i < 362; i += kThreads) sm.tw[i] = mel::kTwiddle400[i];
   for (int i = tid; i < VL_MEL_NNZ; i += kThreads) sm.melw[i] = mel::kMelWeights[i];
   for (int i = tid; i <= kMel; i += kThreads) sm.mel_off[i] = mel::kMelOffset[i];
   for (int i = tid; i < kMel; i += kThreads) sm.mel_lo[i] = mel::kMelLo[i];
+  if (tid <= VL_MEL_GROUPS) sm.group[tid] = mel::kMelGroup[tid];
   __syncthreads();
 
   // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
-  if (tid < kPairs * 20) {
-    const int p = tid / 20, n2 = tid % 20;
-    const float* sa = sm.samples + 2 * p * kHop;
+  const int p = tid / 20, lane20 = tid % 20;
+  cpx x[20];
+  if (fft_thread) {
+    const float* sa = sm.u.samples + 2 * p * kHop;
     const float* sb = sa + kHop;
-    cpx x[20];
 #pragma unroll
     for (int n1 = 0; n1 < 20; ++n1) {
-      const int n = 20 * n1 + n2;
+      const int n = 20 * n1 + lane20;
       const float w = sm.window[n];
       x[n1] = {sa[n] * w, sb[n] * w};
     }
+  }
+  __syncthreads();  // samples consumed: the region now takes the stage-1 output
+  if (fft_thread) {
     dft20(x);
 #pragma unroll
     for (int k1 = 0; k1 < 20; ++k1) {
-      const float2 w = sm.tw[k1 * n2];
+      const float2 w = sm.tw[k1 * lane20];
       const cpx y = cmul_conj(x[k1], w.x, w.y);
-      sm.u.t[p][k1][n2] = make_float2(y.re, y.im);
+      sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
     }
   }
   __syncthreads();
 
   // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
-  if (tid < kPairs * 20) {
-    const int p = tid / 20, k1 = tid % 20;
-    cpx x[20];
+  if (fft_thread) {
 #pragma unroll
     for (int n2 = 0; n2 < 20; ++n2) {
-      const float2 v = sm.u.t[p][k1][n2];
+      const float2 v = sm.u.t[p][lane20][n2];
       x[n2] = {v.x, v.y};
     }
+  }
+  __syncthreads();  // stage-1 output consumed: the region now takes Z
+  if (fft_thread) {
     dft20(x);
 #pragma unroll
-    for (int k2 = 0; k2 < 20; ++k2) sm.z[p][k1 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
+    for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
   }
   __syncthreads();
 
   // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
   for (int i = tid; i < kPairs * kBins; i += kThreads) {
-    const int p = i / kBins, k = i % kBins;
-    const float2 a = sm.z[p][k];
-    const float2 b = sm.z[p][k == 0 ? 0 : 400 - k];
+    const int q = i / kBins, k = i - q * kBins;
+    const float2 a = sm.u.z[q][k];
+    const float2 b = sm.u.z[q][k == 0 ? 0 : 400 - k];
     const float ar = a.x + b.x, ai = a.y - b.y;
     const float br = a.x - b.x, bi = a.y + b.y;
-    sm.u.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
-    sm.u.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
+    sm.p[2 * q][k] = (ar * ar + ai * ai) * 0.25f;
+    sm.p[2 * q + 1][k] = (br * br + bi * bi) * 0.25f;
   }
   __syncthreads();
 
-  // ---- mel projection + log10, tile maximum
+  // ---- mel projection + log10 per (frame, run of bins); lanes = consecutive frames
   float local_max = -INFINITY;
-  float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0;
-  for (int i = tid; i < kMel * kTileFrames; i += kThreads) {
-    const int m = i / kTileFrames, f = i % kTileFrames;
-    const int lo = sm.mel_lo[m];
-    const int beg = sm.mel_off[m], end = sm.mel_off[m + 1];
-    const float* pw = sm.u.p[f] + lo - beg;
-    float acc = 0.f;
-    for (int q = beg; q < end; ++q) acc += sm.melw[q] * pw[q];
-    const float v = log10f(fmaxf(acc, 1e-10f));
-    dst[static_cast<int64_t>(m) * kFrames + f] = v;
-    local_max = fmaxf(local_max, v);
+  if (tid < VL_MEL_GROUPS * kTileFrames) {
+    const int g = tid / kTileFrames, f = tid - g * kTileFrames;
+    const float* pw = sm.p[f];
+    float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + f;
+    const int m_end = sm.group[g + 1];
+    for (int m = sm.group[g]; m < m_end; ++m) {
+      const int beg = sm.mel_off[m], end = sm.mel_off[m + 1];
+      const float* pk = pw + sm.mel_lo[m] - beg;
+      float acc = 0.f;
+      for (int q = beg; q < end; ++q) acc += sm.melw[q] * pk[q];
+      // log10 via the hardware log2: |error| < 1e-6 against log10f on this range
+      const float v = __log2f(fmaxf(acc, 1e-10f)) * 0.30102999566398119521f;
+      dst[static_cast<int64_t>(m) * kFrames] = v;
+      local_max = fmaxf(local_max, v);
+    }
   }
   local_max = warp_max(local_max);
   if ((tid & 31) == 0) sm.red[tid >> 5] = local_max;
@@ -300,7 +314,7 @@ size_t logmel_workspace_bytes(int64_t chunks) {
 
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream) {
-  static_assert(sizeof(MelSmem) <= 113 * 1024, "two tiles must fit one SM");
+  static_assert(sizeof(MelSmem) <= 75 * 1024, "three tiles must fit one SM");
   const size_t smem = sizeof(MelSmem);
   cudaError_t err = enable_large_smem(smem);
   if (err != cudaSuccess) return err;
