@@ -181,6 +181,10 @@ def time_op(fn, iters: int, flush=None) -> float:
     for _ in range(iters):
         if flush is not None:
             flush()
+        # A bounded GPU-side busy wait (~50 us) before the start event gives the
+        # host time to enqueue the op, so the event pair brackets device time
+        # only and not the Python wrapper's launch latency.
+        torch.cuda._sleep(100_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(s)
         fn()

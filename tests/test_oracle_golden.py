@@ -128,6 +128,10 @@ def test_kernel_mel_tables_equal_oracle_tables():
     spec.loader.exec_module(gen)
     committed = (PKG / "csrc" / "mel_tables.inc").read_text()
     assert gen.render() == committed, "mel_tables.inc is stale: rerun gen_mel_tables.py"
+    runs = (PKG / "csrc" / "mel_runs.inc").read_text()
+    assert gen.render_runs() == runs, "mel_runs.inc is stale: rerun gen_mel_tables.py"
+    # the unrolled runs cover every bin exactly once with the CSR taps
+    assert runs.count("log10_floor(acc)") == 128 and runs.count("fmaf(") == len(gen.mel_csr()[2])
     fb = oracle.mel_filterbank_f64().astype(np.float32)  # [201, 128]
     weights = _parse_inc_floats(committed, "kMelWeights")
     lo, offsets, w = gen.mel_csr()

@@ -30,22 +30,36 @@
 #include "mel_tables.inc"
 
 namespace vl {
+namespace mel {
+// log10(max(x, 1e-10)) through the hardware log2 (|error| < 1e-6 here).
+__device__ __forceinline__ float log10_floor(float x) {
+  return __log2f(fmaxf(x, 1e-10f)) * 0.30102999566398119521f;
+}
+}  // namespace mel
+}  // namespace vl
+
+#include "mel_runs.inc"
+
+namespace vl {
 namespace {
 
 constexpr int kChunkSamples = 480000;
 constexpr int kHop = 160;
 constexpr int kPad = 200;
 constexpr int kFrames = 3000;              // frames kept (the 3001st is dropped)
-constexpr int kTileFrames = 24;            // frames per tile (divides 3000)
+constexpr int kTileFrames = 32;            // frames per tile: one per lane in the mel stage
 constexpr int kPairs = kTileFrames / 2;    // complex FFTs per tile
-constexpr int kTilesPerChunk = kFrames / kTileFrames;  // 125
-constexpr int kTileSamples = kHop * (kTileFrames - 1) + 400;  // 4080
+constexpr int kTilesPerChunk = (kFrames + kTileFrames - 1) / kTileFrames;  // 94 (last: 24 frames)
+constexpr int kTileSamples = kHop * (kTileFrames - 1) + 400;  // 5360
 constexpr int kBins = 201;
 constexpr int kMel = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = kPairs * 20;      // 320: one FFT task per thread, 10 warps
 constexpr int kTRow = 21;                  // padded row (complex) of the stage-1 transpose
 constexpr int kNormSlices = 16;            // normalise blocks per chunk
 constexpr int kBatchChunks = 32;           // chunks per L2-resident batch
+constexpr int kMaxTilesPerChunk = 125;     // capacity per chunk of the no-alloc scratch
+static_assert(kTilesPerChunk <= kMaxTilesPerChunk, "no-alloc scratch too small");
+static_assert(VL_MEL_GROUPS == kThreads / 32, "one mel-bin run per warp");
 
 struct MelSmem {
   // samples -> stage-1 output t[p][k1][n2] -> packed spectra z[p][k]; each
@@ -58,10 +72,6 @@ struct MelSmem {
   float p[kTileFrames][kBins];             // power spectra
   float window[400];
   float2 tw[362];                          // W400^m, m <= 19 * 19
-  float melw[VL_MEL_NNZ];
-  int mel_off[kMel + 1];
-  int mel_lo[kMel];
-  int group[VL_MEL_GROUPS + 1];
   float red[kThreads / 32];
 };
 
@@ -120,7 +130,7 @@ __device__ __forceinline__ int reflect(int j) {
   return j;
 }
 
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 2)
     mel_tile_kernel(const float* __restrict__ pcm, float* __restrict__ out,
                     float* __restrict__ tile_max, int chunk0) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -131,9 +141,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int f0 = tile * kTileFrames;
   const float* src = pcm + chunk * kChunkSamples;
   const int j0 = f0 * kHop - kPad;
-  const bool fft_thread = tid < kPairs * 20;
 
-  // ---- stage 0: samples, window, twiddles and filterbank into shared memory
+  // ---- stage 0: samples (reflect-padded at the chunk edges), window, twiddles
   if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
     const float4* s4 = reinterpret_cast<const float4*>(src + j0);
     float4* d4 = reinterpret_cast<float4*>(sm.u.samples);
@@ -143,16 +152,12 @@ __global__ void __launch_bounds__(kThreads, 3)
   }
   for (int i = tid; i < 400; i += kThreads) sm.window[i] = mel::kWindow[i];
   for (int i = tid; i < 362; i += kThreads) sm.tw[i] = mel::kTwiddle400[i];
-  for (int i = tid; i < VL_MEL_NNZ; i += kThreads) sm.melw[i] = mel::kMelWeights[i];
-  for (int i = tid; i <= kMel; i += kThreads) sm.mel_off[i] = mel::kMelOffset[i];
-  for (int i = tid; i < kMel; i += kThreads) sm.mel_lo[i] = mel::kMelLo[i];
-  if (tid <= VL_MEL_GROUPS) sm.group[tid] = mel::kMelGroup[tid];
   __syncthreads();
 
   // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
-  const int p = tid / 20, lane20 = tid % 20;
+  const int p = tid / 20, lane20 = tid - 20 * (tid / 20);
   cpx x[20];
-  if (fft_thread) {
+  {
     const float* sa = sm.u.samples + 2 * p * kHop;
     const float* sb = sa + kHop;
 #pragma unroll
@@ -163,65 +168,59 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   __syncthreads();  // samples consumed: the region now takes the stage-1 output
-  if (fft_thread) {
-    dft20(x);
+  dft20(x);
 #pragma unroll
-    for (int k1 = 0; k1 < 20; ++k1) {
-      const float2 w = sm.tw[k1 * lane20];
-      const cpx y = cmul_conj(x[k1], w.x, w.y);
-      sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
-    }
+  for (int k1 = 0; k1 < 20; ++k1) {
+    const float2 w = sm.tw[k1 * lane20];
+    const cpx y = cmul_conj(x[k1], w.x, w.y);
+    sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
   }
   __syncthreads();
 
   // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
-  if (fft_thread) {
 #pragma unroll
-    for (int n2 = 0; n2 < 20; ++n2) {
-      const float2 v = sm.u.t[p][lane20][n2];
-      x[n2] = {v.x, v.y};
-    }
+  for (int n2 = 0; n2 < 20; ++n2) {
+    const float2 v = sm.u.t[p][lane20][n2];
+    x[n2] = {v.x, v.y};
   }
   __syncthreads();  // stage-1 output consumed: the region now takes Z
-  if (fft_thread) {
-    dft20(x);
+  dft20(x);
 #pragma unroll
-    for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
-  }
+  for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
   __syncthreads();
 
   // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
-  for (int i = tid; i < kPairs * kBins; i += kThreads) {
-    const int q = i / kBins, k = i - q * kBins;
-    const float2 a = sm.u.z[q][k];
-    const float2 b = sm.u.z[q][k == 0 ? 0 : 400 - k];
+  for (int k = lane20; k < kBins; k += 20) {
+    const float2 a = sm.u.z[p][k];
+    const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
     const float ar = a.x + b.x, ai = a.y - b.y;
     const float br = a.x - b.x, bi = a.y + b.y;
-    sm.p[2 * q][k] = (ar * ar + ai * ai) * 0.25f;
-    sm.p[2 * q + 1][k] = (br * br + bi * bi) * 0.25f;
+    sm.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
+    sm.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
   }
   __syncthreads();
 
-  // ---- mel projection + log10 per (frame, run of bins); lanes = consecutive frames
+  // ---- mel projection + log10: warp w = run of bins w, lane = frame
+  const int warp = tid >> 5, lane = tid & 31;
   float local_max = -INFINITY;
-  if (tid < VL_MEL_GROUPS * kTileFrames) {
-    const int g = tid / kTileFrames, f = tid - g * kTileFrames;
-    const float* pw = sm.p[f];
-    float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + f;
-    const int m_end = sm.group[g + 1];
-    for (int m = sm.group[g]; m < m_end; ++m) {
-      const int beg = sm.mel_off[m], end = sm.mel_off[m + 1];
-      const float* pk = pw + sm.mel_lo[m] - beg;
-      float acc = 0.f;
-      for (int q = beg; q < end; ++q) acc += sm.melw[q] * pk[q];
-      // log10 via the hardware log2: |error| < 1e-6 against log10f on this range
-      const float v = __log2f(fmaxf(acc, 1e-10f)) * 0.30102999566398119521f;
-      dst[static_cast<int64_t>(m) * kFrames] = v;
-      local_max = fmaxf(local_max, v);
+  if (f0 + lane < kFrames) {
+    const float* pw = sm.p[lane];
+    float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + lane;
+    switch (warp) {
+      case 0: local_max = mel::mel_run<0>(pw, dst); break;
+      case 1: local_max = mel::mel_run<1>(pw, dst); break;
+      case 2: local_max = mel::mel_run<2>(pw, dst); break;
+      case 3: local_max = mel::mel_run<3>(pw, dst); break;
+      case 4: local_max = mel::mel_run<4>(pw, dst); break;
+      case 5: local_max = mel::mel_run<5>(pw, dst); break;
+      case 6: local_max = mel::mel_run<6>(pw, dst); break;
+      case 7: local_max = mel::mel_run<7>(pw, dst); break;
+      case 8: local_max = mel::mel_run<8>(pw, dst); break;
+      default: local_max = mel::mel_run<9>(pw, dst); break;
     }
   }
   local_max = warp_max(local_max);
-  if ((tid & 31) == 0) sm.red[tid >> 5] = local_max;
+  if (lane == 0) sm.red[warp] = local_max;
   __syncthreads();
   if (tid == 0) {
     float mx = sm.red[0];
@@ -283,7 +282,7 @@ cudaError_t enable_large_smem(size_t smem) {
 // the library so that entry point allocates nothing.  Host code must not
 // use the symbol itself as a pointer (it names a host-side shadow); it
 // fetches the device address once per device with cudaGetSymbolAddress.
-static __device__ __align__(256) float g_noalloc_tile_max[VL_LOGMEL_NOALLOC_MAX_CHUNKS * kTilesPerChunk];
+static __device__ __align__(256) float g_noalloc_tile_max[VL_LOGMEL_NOALLOC_MAX_CHUNKS * kMaxTilesPerChunk];
 
 }  // namespace
 
@@ -314,7 +313,7 @@ size_t logmel_workspace_bytes(int64_t chunks) {
 
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream) {
-  static_assert(sizeof(MelSmem) <= 75 * 1024, "three tiles must fit one SM");
+  static_assert(sizeof(MelSmem) <= 113 * 1024, "two tiles must fit one SM");
   const size_t smem = sizeof(MelSmem);
   cudaError_t err = enable_large_smem(smem);
   if (err != cudaSuccess) return err;

@@ -11,10 +11,12 @@
 //       over the pairs (d, d + rot/2), d < rot/2, of every head.
 // The reference reads cos/sin from host-built tables of 1024 or 1500 rows;
 // here they are evaluated per (token, pair) in fp64 on the device (no table,
-// no position limit) and shared through shared memory by all heads of the
-// token.  Each thread then rotates one 16-byte vector of x1 together with
-// the matching vector of x2, so every head's rotated half moves as whole
-// 16-byte accesses and the untouched half is never read.
+// no position limit).  One warp owns one token: lane l rotates the 16-byte
+// vector l % per_head of the x1 half together with its x2 partner for head
+// l / per_head (+ multiples of 32 / per_head), so indexing is shifts only,
+// the first vectors are requested before the fp64 cos/sin evaluation, and
+// the untouched half of each head is never read.  Shapes whose rotated half
+// is not a power-of-two number of 16-byte vectors use a scalar block kernel.
 #include <cmath>
 
 #include "vl_common.cuh"
@@ -172,6 +174,119 @@ __global__ void __launch_bounds__(kRopeThreads)
   }
 }
 
+constexpr int kWarpRopeWarps = 4;         // tokens per block
+constexpr int kWarpRopePrefetch = 4;      // head iterations requested before cos/sin
+
+template <typename T>
+__device__ __forceinline__ T* head_row(const RopeArgs& a, int64_t r, int h) {
+  return h < a.n_q_heads
+             ? static_cast<T*>(a.q) + r * a.q_row_stride + static_cast<int64_t>(h) * a.head_dim
+             : static_cast<T*>(a.k) + r * a.k_row_stride +
+                   static_cast<int64_t>(h - a.n_q_heads) * a.head_dim;
+}
+
+// PH = 16-byte vectors per rotated half (a power of two <= 32).
+template <typename T, int PH>
+__global__ void __launch_bounds__(kWarpRopeWarps * 32)
+    rope_warp_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq) {
+  using S = Storage<T>;
+  constexpr int E = S::kVec;
+  constexpr int kHalf = PH * E;            // rotary_dim / 2
+  constexpr int kHeadsPerIter = 32 / PH;
+  __shared__ float2 cs_all[kWarpRopeWarps][kHalf];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarpRopeWarps + warp;
+  if (r >= a.tokens) return;
+  const int heads = a.n_q_heads + a.n_k_heads;
+  const int iters = (heads + kHeadsPerIter - 1) / kHeadsPerIter;
+  const int j = lane & (PH - 1);
+  const int hl = lane / PH;
+
+  uint4 x1v[kWarpRopePrefetch], x2v[kWarpRopePrefetch];
+#pragma unroll
+  for (int it = 0; it < kWarpRopePrefetch; ++it) {
+    const int h = it * kHeadsPerIter + hl;
+    if (it < iters && h < heads) {
+      T* row = head_row<T>(a, r, h);
+      x1v[it] = ld_vec(row + j * E);
+      x2v[it] = ld_vec(row + kHalf + j * E);
+    }
+  }
+
+  float2* cs = cs_all[warp];
+  const double pos = static_cast<double>(token_position(a, r));
+  for (int d = lane; d < kHalf; d += 32) {
+    double sn, cn;
+    sincos(pos * freq.v[d], &sn, &cn);
+    cs[d] = make_float2(static_cast<float>(cn), static_cast<float>(sn));
+  }
+  __syncwarp();
+  float c[E], sn[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float2 v = cs[j * E + e];
+    c[e] = v.x;
+    sn[e] = v.y;
+  }
+
+  for (int it0 = 0; it0 < iters; it0 += kWarpRopePrefetch) {
+    if (it0 > 0) {
+#pragma unroll
+      for (int u = 0; u < kWarpRopePrefetch; ++u) {
+        const int h = (it0 + u) * kHeadsPerIter + hl;
+        if (it0 + u < iters && h < heads) {
+          T* row = head_row<T>(a, r, h);
+          x1v[u] = ld_vec(row + j * E);
+          x2v[u] = ld_vec(row + kHalf + j * E);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kWarpRopePrefetch; ++u) {
+      const int h = (it0 + u) * kHeadsPerIter + hl;
+      if (it0 + u < iters && h < heads) {
+        float x1[E], x2[E], y1[E], y2[E];
+        S::unpack(x1v[u], x1);
+        S::unpack(x2v[u], x2);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          y1[e] = x1[e] * c[e] - x2[e] * sn[e];
+          y2[e] = x2[e] * c[e] + x1[e] * sn[e];
+        }
+        T* row = head_row<T>(a, r, h);
+        st_vec(row + j * E, S::pack(y1));
+        st_vec(row + kHalf + j * E, S::pack(y2));
+      }
+    }
+  }
+
+  if (a.v == nullptr) return;
+  // Fused KV append: copy this token's (now rotated) K row and its V row to
+  // the slot; the warp's own stores above are visible after the warp sync.
+  __syncwarp();
+  const int64_t slot = a.slot_mapping[r];
+  if (slot < 0) return;
+  if (slot >= a.num_slots) {
+    if (lane == 0 && a.status) atomicOr(a.status, VL_STATUS_BAD_SLOT);
+    return;
+  }
+  const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
+  const uint4* krow = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + r * a.k_row_stride);
+  const uint4* vrow = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + r * row_elems);
+  uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(a.k_cache) + slot * row_elems);
+  uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(a.v_cache) + slot * row_elems);
+  for (int64_t i = lane; i < row_elems / E; i += 32) {
+    st_vec(kc + i, ld_vec(krow + i));
+    st_vec(vc + i, ld_vec(vrow + i));
+  }
+}
+
+template <typename T, int PH>
+void launch_warp_rope(const RopeArgs& a, const InvFreq& freq, cudaStream_t stream) {
+  const int64_t blocks = (a.tokens + kWarpRopeWarps - 1) / kWarpRopeWarps;
+  rope_warp_kernel<T, PH><<<static_cast<unsigned>(blocks), kWarpRopeWarps * 32, 0, stream>>>(a, freq);
+}
+
 template <typename T>
 cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
   constexpr int E = Storage<T>::kVec;
@@ -193,7 +308,17 @@ cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
   if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;
   const int64_t blocks = (a.tokens + tpb - 1) / tpb;
   const size_t smem = static_cast<size_t>(tpb) * half_rot * sizeof(float2);
-  if (vec)
+  const int per_head = half_rot / E;
+  if (vec && per_head <= 32 && (per_head & (per_head - 1)) == 0) {
+    switch (per_head) {
+      case 1: launch_warp_rope<T, 1>(a, freq, stream); break;
+      case 2: launch_warp_rope<T, 2>(a, freq, stream); break;
+      case 4: launch_warp_rope<T, 4>(a, freq, stream); break;
+      case 8: launch_warp_rope<T, 8>(a, freq, stream); break;
+      case 16: launch_warp_rope<T, 16>(a, freq, stream); break;
+      default: launch_warp_rope<T, 32>(a, freq, stream); break;
+    }
+  } else if (vec)
     rope_kernel<T, true><<<static_cast<unsigned>(blocks), kRopeThreads, smem, stream>>>(
         a, freq, static_cast<int>(tpb));
   else
