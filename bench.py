@@ -174,24 +174,24 @@ def sum_over_ranks(x: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 
 def time_op(fn, iters: int, flush=None) -> float:
-    """Mean device time (ms) of fn over `iters` launches, L2 flushed before each."""
+    """Mean device time (ms) of fn over `iters` launches, L2 flushed before each.
+
+    All iterations are enqueued before the one synchronisation, so the host
+    runs ahead of the GPU and each event pair brackets device time only (no
+    host launch gap)."""
     import torch
     s = torch.cuda.current_stream()
-    total = 0.0
+    pairs = []
     for _ in range(iters):
         if flush is not None:
             flush()
-        # A bounded GPU-side busy wait (~50 us) before the start event gives the
-        # host time to enqueue the op, so the event pair brackets device time
-        # only and not the Python wrapper's launch latency.
-        torch.cuda._sleep(100_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(s)
         fn()
         b.record(s)
-        b.synchronize()
-        total += a.elapsed_time(b)
-    return total / iters
+        pairs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in pairs) / iters
 
 
 def op_table(peak: float, only: str | None = None, iters_override: int | None = None) -> dict:
