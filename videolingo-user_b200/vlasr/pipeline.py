@@ -100,7 +100,13 @@ class EncoderNormChain:
         self.gamma = normal((s.layers, s.hidden), 1.0, 0.02)
         self.beta = normal((s.layers, s.hidden), 0.0, 0.02)
         self.h = normal((s.rows, s.hidden))          # residual stream
-        self.y = normal((s.rows, s.hidden))          # LN output = next layer's delta
+        # LN output = next layer's delta.  Two buffers when sharded: step i's
+        # outputs are all-gathered on a side stream while step i+1 computes
+        # into the other buffer.
+        self.y_bufs = [normal((s.rows, s.hidden))]
+        if world > 1:
+            self.y_bufs.append(normal((s.rows, s.hidden)))
+        self.cur = 0
         self.g_in = normal((s.rows, s.ffn))          # FFN hidden (stand-in for fc1 output)
         self.g_out = torch.empty((s.rows, s.ffn), device=self.device, dtype=bf)
         self.mel = torch.empty((s.chunks, MEL_BINS, MEL_FRAMES), device=self.device,
@@ -108,9 +114,17 @@ class EncoderNormChain:
         self.mel_ws = torch.empty(ops.logmel_workspace_bytes(max(s.chunks, 1)), device=self.device,
                                   dtype=torch.uint8)
         self.y_all = None
+        self.comm = None
+        self.gather_done = [None, None]
         if world > 1:
             self.y_all = torch.empty((self.total_chunks * s.frames, s.hidden), device=self.device,
                                      dtype=bf)
+            self.comm = torch.cuda.Stream(self.device)
+
+    @property
+    def y(self) -> torch.Tensor:
+        """The LN-output buffer of the current step."""
+        return self.y_bufs[self.cur]
 
     # -- launch sequences ---------------------------------------------------
     def launches_per_step(self, groups: int = 1) -> int:
@@ -135,21 +149,55 @@ class EncoderNormChain:
         ops.gelu_erf(self.g_in[r0:r1], out=self.g_out[r0:r1])
 
     def all_gather(self) -> None:
+        """Blocking all-gather of this step's outputs on the current stream."""
         if self.y_all is not None:
             gather_outputs(self.y_all, self.y, self.group)
+
+    def _begin_step(self) -> None:
+        """Before writing this step's buffer: wait until its previous gather is done."""
+        ev = self.gather_done[self.cur]
+        if ev is not None:
+            torch.cuda.current_stream(self.device).wait_event(ev)
+
+    def _end_step(self, timer=None) -> None:
+        """Start the all-gather of this step's outputs on the side stream (it
+        overlaps the next step's kernels) and switch to the other buffer."""
+        if self.world > 1:
+            ready = torch.cuda.Event()
+            ready.record(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(ready)
+                if timer is not None:
+                    timer("all_gather", self.all_gather, self.comm)
+                else:
+                    self.all_gather()
+                done = torch.cuda.Event()
+                done.record(self.comm)
+            self.gather_done[self.cur] = done
+            self.cur = 1 - self.cur
+
+    def finish(self) -> None:
+        """Make the current stream wait for every outstanding all-gather."""
+        cur = torch.cuda.current_stream(self.device)
+        for ev in self.gather_done:
+            if ev is not None:
+                cur.wait_event(ev)
 
     def step(self, pcm: torch.Tensor, timer=None) -> None:
         """One pass over this rank's chunks with device-resident PCM.
 
-        `timer(name, fn)` (optional) wraps each launch, e.g. with CUDA events."""
-        call = timer if timer is not None else (lambda name, fn: fn())
+        `timer(name, fn[, stream])` (optional) wraps each launch, e.g. with
+        CUDA events.  When sharded, the step ends by starting the all-gather
+        of its outputs on a side stream; call finish() before reading y_all."""
+        call = timer if timer is not None else (lambda name, fn, stream=None: fn())
+        self._begin_step()
+        y = self.y
         call("mel", lambda: self.run_mel(pcm))
         for l in range(self.shape.layers):
             call("add_layernorm", lambda l=l: ops.add_layernorm(
-                self.h, self.y, self.gamma[l], self.beta[l], out=self.y))
+                self.h, y, self.gamma[l], self.beta[l], out=y))
             call("gelu", lambda: ops.gelu_erf(self.g_in, out=self.g_out))
-        if self.world > 1:
-            call("all_gather", self.all_gather)
+        self._end_step(timer)
 
     # -- host-buffer path -----------------------------------------------------
     def step_host(self, pcm_host: torch.Tensor, mel_host: torch.Tensor, y_host: torch.Tensor,
@@ -165,6 +213,7 @@ class EncoderNormChain:
         down = torch.cuda.Stream(self.device)
         bounds = [shard_range(s.chunks, g, groups) for g in range(groups)]
         bounds = [b for b in bounds if b[1] > b[0]]
+        self._begin_step()
         uploaded = []
         up.wait_stream(cur)
         with torch.cuda.stream(up):
@@ -185,9 +234,8 @@ class EncoderNormChain:
             with torch.cuda.stream(down):
                 mel_host[c0:c1].copy_(self.mel[c0:c1], non_blocking=True)
                 y_host[r0:r1].copy_(self.y[r0:r1], non_blocking=True)
-        if self.world > 1:
-            self.all_gather()
         cur.wait_stream(down)
+        self._end_step()
 
     def host_bytes_per_step(self) -> tuple[int, int]:
         s = self.shape
