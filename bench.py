@@ -49,6 +49,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-ops", action="store_true", help="skip the per-op roofline table")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--nccl-channels", type=int, default=None,
+                   help="cap NCCL's channels (and so the SMs its all-gather occupies "
+                        "while it overlaps the next step's kernels)")
     p.add_argument("--op", default=None,
                    help="profiling mode: run only this op of the per-op table "
                         "(warmup + steps launches, no flush) and print its timing")
@@ -135,6 +138,8 @@ def init_dist(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import datetime
+        if args.nccl_channels:
+            os.environ["NCCL_MAX_NCHANNELS"] = str(args.nccl_channels)
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -528,6 +533,7 @@ def main() -> None:
                            "step on a side stream (the last one inside the timed region)"
                            if world > 1 else ""),
                        "l2": "inputs larger than L2 (each op streams >= 0.49 GB per launch)",
+                       "nccl_max_nchannels": os.environ.get("NCCL_MAX_NCHANNELS"),
                        "bytes_per_step": bytes_step["total"] * world},
             "roofline": roofline, "kernels": breakdown, "gpu_launches": launches,
             "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "ops": ops,
