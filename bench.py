@@ -52,6 +52,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--nccl-channels", type=int, default=None,
                    help="cap NCCL's channels (and so the SMs its all-gather occupies "
                         "while it overlaps the next step's kernels)")
+    p.add_argument("--gather", choices=["overlap", "blocking"], default="overlap",
+                   help="all-gather each step's outputs on a side stream overlapping the "
+                        "next step (default) or on the compute stream at the end of the step")
     p.add_argument("--op", default=None,
                    help="profiling mode: run only this op of the per-op table "
                         "(warmup + steps launches, no flush) and print its timing")
@@ -409,7 +412,7 @@ def main() -> None:
     shape = ChainShape(chunks=c1 - c0, layers=LAYERS)
     group = None
     chain = EncoderNormChain(shape, dev, seed=0, group=group, world=world, rank=rank,
-                             total_chunks=args.chunks)
+                             total_chunks=args.chunks, overlap_gather=args.gather == "overlap")
     pcm = audio_chunks_device(shape.chunks, c0, 0, dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -529,9 +532,11 @@ def main() -> None:
                        "chunks_per_rank": shape.chunks, "layers": LAYERS,
                        "ln_shape": [1500, 1280], "gelu_shape": [1500, 5120],
                        "parallelism": f"chunk-sharded x{world}" + (
-                           " + NCCL all-gather of each step's outputs, overlapped with the next "
-                           "step on a side stream (the last one inside the timed region)"
-                           if world > 1 else ""),
+                           (" + NCCL all-gather of each step's outputs, overlapped with the next "
+                            "step on a side stream (the last one inside the timed region)")
+                           if args.gather == "overlap" else
+                           " + NCCL all-gather of each step's outputs at the end of the step"
+                           ) if world > 1 else "",
                        "l2": "inputs larger than L2 (each op streams >= 0.49 GB per launch)",
                        "nccl_max_nchannels": os.environ.get("NCCL_MAX_NCHANNELS"),
                        "bytes_per_step": bytes_step["total"] * world},

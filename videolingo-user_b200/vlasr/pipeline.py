@@ -80,13 +80,14 @@ class EncoderNormChain:
     """Resident buffers and launch sequence of one rank's shard."""
 
     def __init__(self, shape: ChainShape, device, seed: int = 0, group=None, world: int = 1,
-                 rank: int = 0, total_chunks: int | None = None):
+                 rank: int = 0, total_chunks: int | None = None, overlap_gather: bool = True):
         self.shape = shape
         self.device = torch.device(device)
         self.group = group
         self.world = world
         self.rank = rank
         self.total_chunks = total_chunks if total_chunks is not None else shape.chunks * world
+        self.overlap_gather = overlap_gather
         s = shape
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed * 7919 + rank)
@@ -104,7 +105,7 @@ class EncoderNormChain:
         # outputs are all-gathered on a side stream while step i+1 computes
         # into the other buffer.
         self.y_bufs = [normal((s.rows, s.hidden))]
-        if world > 1:
+        if world > 1 and overlap_gather:
             self.y_bufs.append(normal((s.rows, s.hidden)))
         self.cur = 0
         self.g_in = normal((s.rows, s.ffn))          # FFN hidden (stand-in for fc1 output)
@@ -162,7 +163,12 @@ class EncoderNormChain:
     def _end_step(self, timer=None) -> None:
         """Start the all-gather of this step's outputs on the side stream (it
         overlaps the next step's kernels) and switch to the other buffer."""
-        if self.world > 1:
+        if self.world > 1 and not self.overlap_gather:
+            if timer is not None:
+                timer("all_gather", self.all_gather)
+            else:
+                self.all_gather()
+        elif self.world > 1:
             ready = torch.cuda.Event()
             ready.record(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
