@@ -62,10 +62,10 @@ static_assert(kTilesPerChunk <= kMaxTilesPerChunk, "no-alloc scratch too small")
 static_assert(VL_MEL_GROUPS == kThreads / 32, "one mel-bin run per warp");
 
 struct MelSmem {
-  // samples -> stage-1 output t[p][k1][n2] -> packed spectra z[p][k]; each
-  // stage reads its input into registers and passes a barrier before writing.
+  float samples[kTileSamples];             // next tile's samples, filled by cp.async
+  // stage-1 output t[p][k1][n2] -> packed spectra z[p][k]; stage 2 reads t
+  // into registers and passes a barrier before writing z.
   union {
-    float samples[kTileSamples];
     float2 t[kPairs][20][kTRow];
     float2 z[kPairs][400];
   } u;
@@ -74,6 +74,17 @@ struct MelSmem {
   float2 tw[362];                          // W400^m, m <= 19 * 19
   float red[kThreads / 32];
 };
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 struct cpx {
   float re, im;
@@ -130,104 +141,121 @@ __device__ __forceinline__ int reflect(int j) {
   return j;
 }
 
+// Asynchronous copy of one tile's samples (reflect-padded at the chunk edges)
+// into shared memory; the copy overlaps the previous tile's compute.
+__device__ __forceinline__ void prefetch_samples(float* dst, const float* __restrict__ pcm,
+                                                 int64_t chunk, int tile, int tid) {
+  const float* src = pcm + chunk * kChunkSamples;
+  const int j0 = tile * kTileFrames * kHop - kPad;
+  if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
+    for (int i = tid; i < kTileSamples / 4; i += kThreads) cp_async16(dst + 4 * i, src + j0 + 4 * i);
+  } else {
+    for (int i = tid; i < kTileSamples; i += kThreads) cp_async4(dst + i, src + reflect(j0 + i));
+  }
+  cp_async_commit();
+}
+
+// Persistent: each block walks tiles blockIdx.x, +gridDim.x, ... of the batch
+// (chunk-major), prefetching the next tile's samples while it computes.
 __global__ void __launch_bounds__(kThreads, 2)
     mel_tile_kernel(const float* __restrict__ pcm, float* __restrict__ out,
-                    float* __restrict__ tile_max, int chunk0) {
+                    float* __restrict__ tile_max, int chunk0, int n_chunks) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   MelSmem& sm = *reinterpret_cast<MelSmem*>(smem_raw);
   const int tid = threadIdx.x;
-  const int tile = blockIdx.x;
-  const int64_t chunk = chunk0 + blockIdx.y;
-  const int f0 = tile * kTileFrames;
-  const float* src = pcm + chunk * kChunkSamples;
-  const int j0 = f0 * kHop - kPad;
-
-  // ---- stage 0: samples (reflect-padded at the chunk edges), window, twiddles
-  if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
-    const float4* s4 = reinterpret_cast<const float4*>(src + j0);
-    float4* d4 = reinterpret_cast<float4*>(sm.u.samples);
-    for (int i = tid; i < kTileSamples / 4; i += kThreads) d4[i] = __ldcs(s4 + i);
-  } else {
-    for (int i = tid; i < kTileSamples; i += kThreads) sm.u.samples[i] = src[reflect(j0 + i)];
-  }
+  const int total = n_chunks * kTilesPerChunk;
+  int w = blockIdx.x;
+  if (w < total) prefetch_samples(sm.samples, pcm, chunk0 + w / kTilesPerChunk, w % kTilesPerChunk, tid);
   for (int i = tid; i < 400; i += kThreads) sm.window[i] = mel::kWindow[i];
   for (int i = tid; i < 362; i += kThreads) sm.tw[i] = mel::kTwiddle400[i];
-  __syncthreads();
-
-  // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
   const int p = tid / 20, lane20 = tid - 20 * (tid / 20);
-  cpx x[20];
-  {
-    const float* sa = sm.u.samples + 2 * p * kHop;
-    const float* sb = sa + kHop;
-#pragma unroll
-    for (int n1 = 0; n1 < 20; ++n1) {
-      const int n = 20 * n1 + lane20;
-      const float w = sm.window[n];
-      x[n1] = {sa[n] * w, sb[n] * w};
-    }
-  }
-  __syncthreads();  // samples consumed: the region now takes the stage-1 output
-  dft20(x);
-#pragma unroll
-  for (int k1 = 0; k1 < 20; ++k1) {
-    const float2 w = sm.tw[k1 * lane20];
-    const cpx y = cmul_conj(x[k1], w.x, w.y);
-    sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
-  }
-  __syncthreads();
-
-  // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
-#pragma unroll
-  for (int n2 = 0; n2 < 20; ++n2) {
-    const float2 v = sm.u.t[p][lane20][n2];
-    x[n2] = {v.x, v.y};
-  }
-  __syncthreads();  // stage-1 output consumed: the region now takes Z
-  dft20(x);
-#pragma unroll
-  for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
-  __syncthreads();
-
-  // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
-  for (int k = lane20; k < kBins; k += 20) {
-    const float2 a = sm.u.z[p][k];
-    const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
-    const float ar = a.x + b.x, ai = a.y - b.y;
-    const float br = a.x - b.x, bi = a.y + b.y;
-    sm.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
-    sm.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
-  }
-  __syncthreads();
-
-  // ---- mel projection + log10: warp w = run of bins w, lane = frame
   const int warp = tid >> 5, lane = tid & 31;
-  float local_max = -INFINITY;
-  if (f0 + lane < kFrames) {
-    const float* pw = sm.p[lane];
-    float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + lane;
-    switch (warp) {
-      case 0: local_max = mel::mel_run<0>(pw, dst); break;
-      case 1: local_max = mel::mel_run<1>(pw, dst); break;
-      case 2: local_max = mel::mel_run<2>(pw, dst); break;
-      case 3: local_max = mel::mel_run<3>(pw, dst); break;
-      case 4: local_max = mel::mel_run<4>(pw, dst); break;
-      case 5: local_max = mel::mel_run<5>(pw, dst); break;
-      case 6: local_max = mel::mel_run<6>(pw, dst); break;
-      case 7: local_max = mel::mel_run<7>(pw, dst); break;
-      case 8: local_max = mel::mel_run<8>(pw, dst); break;
-      default: local_max = mel::mel_run<9>(pw, dst); break;
+
+  for (; w < total; w += gridDim.x) {
+    const int64_t chunk = chunk0 + w / kTilesPerChunk;
+    const int tile = w % kTilesPerChunk;
+    const int f0 = tile * kTileFrames;
+    cp_async_wait_all();
+    __syncthreads();  // this tile's samples (and, first time, the tables) are in smem
+
+    // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
+    cpx x[20];
+    {
+      const float* sa = sm.samples + 2 * p * kHop;
+      const float* sb = sa + kHop;
+#pragma unroll
+      for (int n1 = 0; n1 < 20; ++n1) {
+        const int n = 20 * n1 + lane20;
+        const float wv = sm.window[n];
+        x[n1] = {sa[n] * wv, sb[n] * wv};
+      }
+    }
+    __syncthreads();  // samples consumed: start fetching the next tile's
+    if (w + static_cast<int>(gridDim.x) < total) {
+      const int nw = w + gridDim.x;
+      prefetch_samples(sm.samples, pcm, chunk0 + nw / kTilesPerChunk, nw % kTilesPerChunk, tid);
+    }
+    dft20(x);
+#pragma unroll
+    for (int k1 = 0; k1 < 20; ++k1) {
+      const float2 tw = sm.tw[k1 * lane20];
+      const cpx y = cmul_conj(x[k1], tw.x, tw.y);
+      sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
+    }
+    __syncthreads();
+
+    // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
+#pragma unroll
+    for (int n2 = 0; n2 < 20; ++n2) {
+      const float2 v = sm.u.t[p][lane20][n2];
+      x[n2] = {v.x, v.y};
+    }
+    __syncthreads();  // stage-1 output consumed: the region now takes Z
+    dft20(x);
+#pragma unroll
+    for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
+    __syncthreads();
+
+    // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
+    for (int k = lane20; k < kBins; k += 20) {
+      const float2 a = sm.u.z[p][k];
+      const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
+      const float ar = a.x + b.x, ai = a.y - b.y;
+      const float br = a.x - b.x, bi = a.y + b.y;
+      sm.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
+      sm.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
+    }
+    __syncthreads();
+
+    // ---- mel projection + log10: warp w = run of bins w, lane = frame
+    float local_max = -INFINITY;
+    if (f0 + lane < kFrames) {
+      const float* pw = sm.p[lane];
+      float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + lane;
+      switch (warp) {
+        case 0: local_max = mel::mel_run<0>(pw, dst); break;
+        case 1: local_max = mel::mel_run<1>(pw, dst); break;
+        case 2: local_max = mel::mel_run<2>(pw, dst); break;
+        case 3: local_max = mel::mel_run<3>(pw, dst); break;
+        case 4: local_max = mel::mel_run<4>(pw, dst); break;
+        case 5: local_max = mel::mel_run<5>(pw, dst); break;
+        case 6: local_max = mel::mel_run<6>(pw, dst); break;
+        case 7: local_max = mel::mel_run<7>(pw, dst); break;
+        case 8: local_max = mel::mel_run<8>(pw, dst); break;
+        default: local_max = mel::mel_run<9>(pw, dst); break;
+      }
+    }
+    local_max = warp_max(local_max);
+    if (lane == 0) sm.red[warp] = local_max;
+    __syncthreads();
+    if (tid == 0) {
+      float mx = sm.red[0];
+#pragma unroll
+      for (int v = 1; v < kThreads / 32; ++v) mx = fmaxf(mx, sm.red[v]);
+      tile_max[chunk * kTilesPerChunk + tile] = mx;
     }
   }
-  local_max = warp_max(local_max);
-  if (lane == 0) sm.red[warp] = local_max;
-  __syncthreads();
-  if (tid == 0) {
-    float mx = sm.red[0];
-#pragma unroll
-    for (int w = 1; w < kThreads / 32; ++w) mx = fmaxf(mx, sm.red[w]);
-    tile_max[chunk * kTilesPerChunk + tile] = mx;
-  }
+  cp_async_wait_all();
 }
 
 // Fold the chunk's tile maxima, then out = (max(x, max - 8) + 4) / 4 over a
@@ -319,8 +347,10 @@ cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* t
   if (err != cudaSuccess) return err;
   for (int64_t c0 = 0; c0 < chunks; c0 += kBatchChunks) {
     const int64_t n = chunks - c0 < kBatchChunks ? chunks - c0 : kBatchChunks;
-    mel_tile_kernel<<<dim3(kTilesPerChunk, static_cast<unsigned>(n)), kThreads, smem, stream>>>(
-        pcm, out, tile_max, static_cast<int>(c0));
+    int blocks = resident_blocks(reinterpret_cast<const void*>(mel_tile_kernel), kThreads, smem);
+    if (blocks > n * kTilesPerChunk) blocks = static_cast<int>(n * kTilesPerChunk);
+    mel_tile_kernel<<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(
+        pcm, out, tile_max, static_cast<int>(c0), static_cast<int>(n));
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     mel_normalize_kernel<<<dim3(kNormSlices, static_cast<unsigned>(n)), kThreads, 0, stream>>>(

@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kRopeThreads)
 }
 
 constexpr int kWarpRopeWarps = 4;         // tokens per block
-constexpr int kWarpRopePrefetch = 4;      // head iterations requested before cos/sin
+constexpr int kWarpRopePrefetch = 3;      // head iterations requested before cos/sin
 
 template <typename T>
 __device__ __forceinline__ T* head_row(const RopeArgs& a, int64_t r, int h) {
@@ -187,7 +187,7 @@ __device__ __forceinline__ T* head_row(const RopeArgs& a, int64_t r, int h) {
 
 // PH = 16-byte vectors per rotated half (a power of two <= 32).
 template <typename T, int PH>
-__global__ void __launch_bounds__(kWarpRopeWarps * 32)
+__global__ void __launch_bounds__(kWarpRopeWarps * 32, 8)
     rope_warp_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq) {
   using S = Storage<T>;
   constexpr int E = S::kVec;
