@@ -212,9 +212,10 @@ VL_EXPORT int vl_swiglu(const void* gate, const void* up, void* out, int64_t row
  * with n_k_heads == 0).  For every head the first `rotary_dim` dims rotate
  * in pairs (d, d + rotary_dim/2):
  *   x1' = x1*cos - x2*sin,  x2' = x2*cos + x1*sin   (fp32, one rounding)
- * with angle = pos * base^(-2d/rotary_dim) and cos/sin evaluated in fp64 and
- * rounded to fp32, as the reference's host tables are
- * (native/asr/src/engine.cu:892-905, native/asr/src/decoder.cu:950-961).
+ * with angle = pos * base^(-2d/rotary_dim) formed in fp64 as the reference's
+ * host tables are (native/asr/src/engine.cu:892-905,
+ * native/asr/src/decoder.cu:950-961), reduced modulo 2*pi in fp64 and
+ * evaluated with fp32 sincosf (within 3e-7 of the tables' fp32 values).
  * Dims >= rotary_dim are untouched.
  *
  * Position of row r:
