@@ -11,7 +11,8 @@
 //   samples (reflect-padded) -> shared memory
 //   two real frames packed as one complex 400-point FFT (x_a + i*x_b),
 //     400 = 20 x 20: stage 1 = 20 DFT-20s over stride-20 samples + W400
-//     twiddles, stage 2 = 20 DFT-20s (each DFT-20 = 4 x 5 in registers)
+//     twiddles, stage 2 = 20 DFT-20s (each DFT-20 = 4 x 5 in registers, in
+//     packed fp32x2 arithmetic: one instruction per complex add/fma)
 //   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry
 //   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense),
 //     one task per (frame, run of mel bins) with runs of equal cost
@@ -86,52 +87,89 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-struct cpx {
-  float re, im;
+// Complex value (re, im) in one 64-bit register pair, operated on with the
+// sm_100 packed fp32x2 instructions: a complex add, subtract or
+// multiply-add by a real pair is a single instruction.
+struct c2 {
+  unsigned long long v;
 };
-__device__ __forceinline__ cpx cadd(cpx a, cpx b) { return {a.re + b.re, a.im + b.im}; }
-__device__ __forceinline__ cpx csub(cpx a, cpx b) { return {a.re - b.re, a.im - b.im}; }
+__device__ __forceinline__ c2 mk(float re, float im) {
+  c2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(re), "f"(im));
+  return r;
+}
+__device__ __forceinline__ float2 split(c2 a) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a.v));
+  return r;
+}
+__device__ __forceinline__ c2 add(c2 a, c2 b) {
+  c2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ c2 sub(c2 a, c2 b) {
+  c2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ c2 mul(c2 a, c2 b) {
+  c2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ c2 fma2(c2 a, c2 b, c2 c) {  // a * b + c, per lane of the pair
+  c2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+__device__ __forceinline__ c2 swap(c2 a) {
+  const float2 f = split(a);
+  return mk(f.y, f.x);
+}
+// a - i*b and a + i*b
+__device__ __forceinline__ c2 sub_i(c2 a, c2 b) { return fma2(swap(b), mk(1.f, -1.f), a); }
+__device__ __forceinline__ c2 add_i(c2 a, c2 b) { return fma2(swap(b), mk(-1.f, 1.f), a); }
 // a * conj(w) with w = (cos, sin): multiplies by exp(-i*theta).
-__device__ __forceinline__ cpx cmul_conj(cpx a, float c, float s) {
-  return {a.re * c + a.im * s, a.im * c - a.re * s};
+__device__ __forceinline__ c2 cmul_conj(c2 a, float c, float s) {
+  return fma2(swap(a), mk(s, -s), mul(a, mk(c, c)));
 }
 
 // In-place forward DFT of 20 complex points: X[k] = sum_n x[n] exp(-2 pi i k n / 20).
 // 20 = 4 x 5: n = 5a + b, k = c + 4d.  DFT-4 over a, twiddle W20^(b c),
 // DFT-5 over b.
-__device__ __forceinline__ void dft20(cpx (&x)[20]) {
-  cpx u[5][4];
+__device__ __forceinline__ void dft20(c2 (&x)[20]) {
+  c2 u[5][4];
 #pragma unroll
   for (int b = 0; b < 5; ++b) {
-    const cpx x0 = x[b], x1 = x[5 + b], x2 = x[10 + b], x3 = x[15 + b];
-    const cpx t0 = cadd(x0, x2), t1 = csub(x0, x2), t2 = cadd(x1, x3), t3 = csub(x1, x3);
-    u[b][0] = cadd(t0, t2);
-    u[b][2] = csub(t0, t2);
-    u[b][1] = {t1.re + t3.im, t1.im - t3.re};  // t1 - i t3
-    u[b][3] = {t1.re - t3.im, t1.im + t3.re};  // t1 + i t3
+    const c2 t0 = add(x[b], x[10 + b]), t1 = sub(x[b], x[10 + b]);
+    const c2 t2 = add(x[5 + b], x[15 + b]), t3 = sub(x[5 + b], x[15 + b]);
+    u[b][0] = add(t0, t2);
+    u[b][2] = sub(t0, t2);
+    u[b][1] = sub_i(t1, t3);
+    u[b][3] = add_i(t1, t3);
   }
 #pragma unroll
   for (int b = 1; b < 5; ++b)
 #pragma unroll
-    for (int c = 1; c < 4; ++c) {
-      const int j = b * c;
-      u[b][c] = cmul_conj(u[b][c], mel::w20_cos(j), mel::w20_sin(j));
-    }
+    for (int c = 1; c < 4; ++c) u[b][c] = cmul_conj(u[b][c], mel::w20_cos(b * c), mel::w20_sin(b * c));
+  const c2 C1 = mk(mel::kC1, mel::kC1), C2 = mk(mel::kC2, mel::kC2);
+  const c2 S1 = mk(mel::kS1, mel::kS1), S2 = mk(mel::kS2, mel::kS2);
+  const c2 NS1 = mk(-mel::kS1, -mel::kS1);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const cpx x0 = u[0][c], x1 = u[1][c], x2 = u[2][c], x3 = u[3][c], x4 = u[4][c];
-    const cpx a1 = cadd(x1, x4), a2 = cadd(x2, x3), b1 = csub(x1, x4), b2 = csub(x2, x3);
-    const cpx m1 = {x0.re + mel::kC1 * a1.re + mel::kC2 * a2.re,
-                    x0.im + mel::kC1 * a1.im + mel::kC2 * a2.im};
-    const cpx m2 = {x0.re + mel::kC2 * a1.re + mel::kC1 * a2.re,
-                    x0.im + mel::kC2 * a1.im + mel::kC1 * a2.im};
-    const cpx n1 = {mel::kS1 * b1.re + mel::kS2 * b2.re, mel::kS1 * b1.im + mel::kS2 * b2.im};
-    const cpx n2 = {mel::kS2 * b1.re - mel::kS1 * b2.re, mel::kS2 * b1.im - mel::kS1 * b2.im};
-    x[c] = {x0.re + a1.re + a2.re, x0.im + a1.im + a2.im};
-    x[c + 4] = {m1.re + n1.im, m1.im - n1.re};    // m1 - i n1
-    x[c + 16] = {m1.re - n1.im, m1.im + n1.re};   // m1 + i n1
-    x[c + 8] = {m2.re + n2.im, m2.im - n2.re};    // m2 - i n2
-    x[c + 12] = {m2.re - n2.im, m2.im + n2.re};   // m2 + i n2
+    const c2 x0 = u[0][c];
+    const c2 a1 = add(u[1][c], u[4][c]), a2 = add(u[2][c], u[3][c]);
+    const c2 b1 = sub(u[1][c], u[4][c]), b2 = sub(u[2][c], u[3][c]);
+    const c2 m1 = fma2(a2, C2, fma2(a1, C1, x0));
+    const c2 m2 = fma2(a2, C1, fma2(a1, C2, x0));
+    const c2 n1 = fma2(b2, S2, mul(b1, S1));
+    const c2 n2 = fma2(b2, NS1, mul(b1, S2));
+    x[c] = add(x0, add(a1, a2));
+    x[c + 4] = sub_i(m1, n1);
+    x[c + 16] = add_i(m1, n1);
+    x[c + 8] = sub_i(m2, n2);
+    x[c + 12] = add_i(m2, n2);
   }
 }
 
@@ -179,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();  // this tile's samples (and, first time, the tables) are in smem
 
     // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
-    cpx x[20];
+    c2 x[20];
     {
       const float* sa = sm.samples + 2 * p * kHop;
       const float* sb = sa + kHop;
@@ -187,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int n1 = 0; n1 < 20; ++n1) {
         const int n = 20 * n1 + lane20;
         const float wv = sm.window[n];
-        x[n1] = {sa[n] * wv, sb[n] * wv};
+        x[n1] = mul(mk(sa[n], sb[n]), mk(wv, wv));
       }
     }
     __syncthreads();  // samples consumed: start fetching the next tile's
@@ -199,21 +237,20 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int k1 = 0; k1 < 20; ++k1) {
       const float2 tw = sm.tw[k1 * lane20];
-      const cpx y = cmul_conj(x[k1], tw.x, tw.y);
-      sm.u.t[p][k1][lane20] = make_float2(y.re, y.im);
+      *reinterpret_cast<unsigned long long*>(&sm.u.t[p][k1][lane20]) =
+          cmul_conj(x[k1], tw.x, tw.y).v;
     }
     __syncthreads();
 
     // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
 #pragma unroll
-    for (int n2 = 0; n2 < 20; ++n2) {
-      const float2 v = sm.u.t[p][lane20][n2];
-      x[n2] = {v.x, v.y};
-    }
+    for (int n2 = 0; n2 < 20; ++n2)
+      x[n2].v = *reinterpret_cast<const unsigned long long*>(&sm.u.t[p][lane20][n2]);
     __syncthreads();  // stage-1 output consumed: the region now takes Z
     dft20(x);
 #pragma unroll
-    for (int k2 = 0; k2 < 20; ++k2) sm.u.z[p][lane20 + 20 * k2] = make_float2(x[k2].re, x[k2].im);
+    for (int k2 = 0; k2 < 20; ++k2)
+      *reinterpret_cast<unsigned long long*>(&sm.u.z[p][lane20 + 20 * k2]) = x[k2].v;
     __syncthreads();
 
     // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
