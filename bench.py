@@ -401,7 +401,7 @@ def main() -> None:
             raise SystemExit(f"unknown op {args.op}")
         print(json.dumps({"op": args.op, **rows[args.op]}), flush=True)
         return
-    from vlasr.pipeline import ChainShape, EncoderNormChain, shard_range
+    from vlasr.pipeline import ChainShape, EncoderNormChain, host_group_bounds, shard_range
     from vlasr.synth import audio_chunks_device
 
     world, rank, local = init_dist(args)
@@ -507,7 +507,8 @@ def main() -> None:
         h2d, d2h = chain.host_bytes_per_step()
         e2e = {"value": round(audio_s / (e_ms / 1e3), 1), "unit": "audio-s/s",
                "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
-               "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)), "groups": groups,
+               "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
+               "groups": len(host_group_bounds(shape.chunks, groups)),
                "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)"}
         del pcm_host, mel_host, y_host, pcm_dev
 

@@ -192,7 +192,8 @@ VL_EXPORT int vl_gelu_erf(const void* in, const void* bias, void* out, int64_t r
                 int64_t cols, int dtype, void* stream);
 
 /*
- * SwiGLU: out = round(g / (1 + exp(-g)) * u) with g = gate, u = up.
+ * SwiGLU: out = round(g / (1 + exp(-g)) * u) with g = gate, u = up (the
+ * division by a fast reciprocal, within 2 ulp of IEEE division in fp32).
  * Replaces silu_mul_kernel (native/asr/src/decoder.cu:103-109), which writes
  * into the gate buffer (out == gate is allowed).  Row strides are in
  * elements, so a packed [rows, 2*cols] gate|up buffer is expressed as

@@ -19,7 +19,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from vlasr.pipeline import gather_outputs, shard_range
+from vlasr.pipeline import gather_outputs, host_group_bounds, shard_range
 
 
 def _free_port() -> int:
@@ -114,3 +114,13 @@ def test_unequal_shards_are_rejected():
             gather_outputs(torch.empty(5, 4), torch.empty(2, 4))
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("chunks,groups", [(256, 8), (32, 4), (128, 8), (3, 4), (1, 1), (8, 8), (7, 3)])
+def test_host_pipeline_groups_tile_the_chunks(chunks, groups):
+    b = host_group_bounds(chunks, groups)
+    assert b[0][0] == 0 and b[-1][1] == chunks
+    assert all(x[1] == y[0] and y[1] > y[0] for x, y in zip(b, b[1:]))
+    if len(b) > 2:  # half-size first and last groups
+        assert b[0][1] - b[0][0] <= b[1][1] - b[1][0]
+        assert b[-1][1] - b[-1][0] <= b[-2][1] - b[-2][0]

@@ -69,6 +69,20 @@ def gather_outputs(full: torch.Tensor, shard: torch.Tensor, group=None) -> None:
     dist.all_gather_into_tensor(full, shard.contiguous(), group=group)
 
 
+def host_group_bounds(chunks: int, groups: int) -> list[tuple[int, int]]:
+    """Chunk groups of the host-buffer pipeline: `groups` equal middle groups
+    plus a half-size first and last group, so the upload that nothing
+    overlaps (the first) and the download that nothing overlaps (the last)
+    are short."""
+    if groups <= 1 or chunks < 4:
+        return [(0, chunks)]
+    edge = max(1, chunks // (2 * groups))
+    inner = [shard_range(chunks - 2 * edge, g, groups - 1) for g in range(groups - 1)]
+    bounds = [(0, edge)] + [(edge + a, edge + b) for a, b in inner if b > a]
+    bounds.append((chunks - edge, chunks))
+    return bounds
+
+
 def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous chunk range [begin, end) of `rank`; equal shares when world divides total."""
     base, extra = divmod(total, world)
@@ -217,8 +231,7 @@ class EncoderNormChain:
         cur = torch.cuda.current_stream(self.device)
         up = torch.cuda.Stream(self.device)
         down = torch.cuda.Stream(self.device)
-        bounds = [shard_range(s.chunks, g, groups) for g in range(groups)]
-        bounds = [b for b in bounds if b[1] > b[0]]
+        bounds = host_group_bounds(s.chunks, groups)
         self._begin_step()
         uploaded = []
         up.wait_stream(cur)
