@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kRopeThreads)
 }
 
 constexpr int kWarpRopeWarps = 4;         // tokens per block
-constexpr int kWarpRopePrefetch = 4;      // head iterations requested before cos/sin
+constexpr int kWarpRopePrefetch = 3;      // head iterations of a token requested ahead
 
 template <typename T>
 __device__ __forceinline__ T* head_row(const RopeArgs& a, int64_t r, int h) {
@@ -201,6 +201,10 @@ __device__ __forceinline__ T* head_row(const RopeArgs& a, int64_t r, int h) {
 }
 
 // PH = 16-byte vectors per rotated half (a power of two <= 32).
+// PH = 16-byte vectors per rotated half (a power of two <= 32).  Persistent:
+// warp w handles tokens w, w + total warps, ...; the next token's vectors are
+// requested before the current token is rotated, so HBM latency overlaps
+// the cos/sin evaluation and the rotation of the previous token.
 template <typename T, int PH>
 __global__ void __launch_bounds__(kWarpRopeWarps * 32)
     rope_warp_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq) {
@@ -208,93 +212,110 @@ __global__ void __launch_bounds__(kWarpRopeWarps * 32)
   constexpr int E = S::kVec;
   constexpr int kHalf = PH * E;            // rotary_dim / 2
   constexpr int kHeadsPerIter = 32 / PH;
+  constexpr int P = kWarpRopePrefetch;
   __shared__ float2 cs_all[kWarpRopeWarps][kHalf];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarpRopeWarps + warp;
+  int64_t r = static_cast<int64_t>(blockIdx.x) * kWarpRopeWarps + warp;
   if (r >= a.tokens) return;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarpRopeWarps;
   const int heads = a.n_q_heads + a.n_k_heads;
   const int iters = (heads + kHeadsPerIter - 1) / kHeadsPerIter;
   const int j = lane & (PH - 1);
   const int hl = lane / PH;
-
-  uint4 x1v[kWarpRopePrefetch], x2v[kWarpRopePrefetch];
-#pragma unroll
-  for (int it = 0; it < kWarpRopePrefetch; ++it) {
-    const int h = it * kHeadsPerIter + hl;
-    if (it < iters && h < heads) {
-      T* row = head_row<T>(a, r, h);
-      x1v[it] = ld_vec(row + j * E);
-      x2v[it] = ld_vec(row + kHalf + j * E);
-    }
-  }
-
   float2* cs = cs_all[warp];
-  const double pos = static_cast<double>(token_position(a, r));
-  for (int d = lane; d < kHalf; d += 32) cs[d] = rope_cos_sin(pos * freq.v[d]);
-  __syncwarp();
-  float c[E], sn[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float2 v = cs[j * E + e];
-    c[e] = v.x;
-    sn[e] = v.y;
-  }
 
-  for (int it0 = 0; it0 < iters; it0 += kWarpRopePrefetch) {
-    if (it0 > 0) {
+  uint4 x1v[P], x2v[P], n1v[P], n2v[P];
+  auto load = [&](int64_t tok, uint4 (&d1)[P], uint4 (&d2)[P]) {
 #pragma unroll
-      for (int u = 0; u < kWarpRopePrefetch; ++u) {
-        const int h = (it0 + u) * kHeadsPerIter + hl;
-        if (it0 + u < iters && h < heads) {
-          T* row = head_row<T>(a, r, h);
-          x1v[u] = ld_vec(row + j * E);
-          x2v[u] = ld_vec(row + kHalf + j * E);
-        }
+    for (int it = 0; it < P; ++it) {
+      const int h = it * kHeadsPerIter + hl;
+      if (it < iters && h < heads) {
+        T* row = head_row<T>(a, tok, h);
+        d1[it] = ld_vec(row + j * E);
+        d2[it] = ld_vec(row + kHalf + j * E);
       }
     }
+  };
+  load(r, x1v, x2v);
+
+  for (;;) {
+    const int64_t rn = r + stride;
+    const double pos = static_cast<double>(token_position(a, r));
+    for (int d = lane; d < kHalf; d += 32) cs[d] = rope_cos_sin(pos * freq.v[d]);
+    __syncwarp();
+    float c[E], sn[E];
 #pragma unroll
-    for (int u = 0; u < kWarpRopePrefetch; ++u) {
-      const int h = (it0 + u) * kHeadsPerIter + hl;
-      if (it0 + u < iters && h < heads) {
-        float x1[E], x2[E], y1[E], y2[E];
-        S::unpack(x1v[u], x1);
-        S::unpack(x2v[u], x2);
+    for (int e = 0; e < E; ++e) {
+      const float2 v = cs[j * E + e];
+      c[e] = v.x;
+      sn[e] = v.y;
+    }
+    if (rn < a.tokens) load(rn, n1v, n2v);
+
+    auto rotate = [&](int h, const uint4& v1, const uint4& v2) {
+      float x1[E], x2[E], y1[E], y2[E];
+      S::unpack(v1, x1);
+      S::unpack(v2, x2);
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          y1[e] = x1[e] * c[e] - x2[e] * sn[e];
-          y2[e] = x2[e] * c[e] + x1[e] * sn[e];
-        }
+      for (int e = 0; e < E; ++e) {
+        y1[e] = x1[e] * c[e] - x2[e] * sn[e];
+        y2[e] = x2[e] * c[e] + x1[e] * sn[e];
+      }
+      T* row = head_row<T>(a, r, h);
+      st_vec(row + j * E, S::pack(y1));
+      st_vec(row + kHalf + j * E, S::pack(y2));
+    };
+#pragma unroll
+    for (int it = 0; it < P; ++it) {
+      const int h = it * kHeadsPerIter + hl;
+      if (it < iters && h < heads) rotate(h, x1v[it], x2v[it]);
+    }
+    for (int it = P; it < iters; ++it) {  // heads beyond the prefetch depth
+      const int h = it * kHeadsPerIter + hl;
+      if (h < heads) {
         T* row = head_row<T>(a, r, h);
-        st_vec(row + j * E, S::pack(y1));
-        st_vec(row + kHalf + j * E, S::pack(y2));
+        rotate(h, ld_vec(row + j * E), ld_vec(row + kHalf + j * E));
       }
     }
-  }
 
-  if (a.v == nullptr) return;
-  // Fused KV append: copy this token's (now rotated) K row and its V row to
-  // the slot; the warp's own stores above are visible after the warp sync.
-  __syncwarp();
-  const int64_t slot = a.slot_mapping[r];
-  if (slot < 0) return;
-  if (slot >= a.num_slots) {
-    if (lane == 0 && a.status) atomicOr(a.status, VL_STATUS_BAD_SLOT);
-    return;
-  }
-  const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
-  const uint4* krow = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + r * a.k_row_stride);
-  const uint4* vrow = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + r * row_elems);
-  uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(a.k_cache) + slot * row_elems);
-  uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(a.v_cache) + slot * row_elems);
-  for (int64_t i = lane; i < row_elems / E; i += 32) {
-    st_vec(kc + i, ld_vec(krow + i));
-    st_vec(vc + i, ld_vec(vrow + i));
+    if (a.v != nullptr) {
+      // Fused KV append: copy this token's (now rotated) K row and its V row
+      // to the slot; the warp's own stores above are visible after the sync.
+      __syncwarp();
+      const int64_t slot = a.slot_mapping[r];
+      if (slot >= a.num_slots) {
+        if (lane == 0 && a.status) atomicOr(a.status, VL_STATUS_BAD_SLOT);
+      } else if (slot >= 0) {
+        const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
+        const uint4* krow =
+            reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + r * a.k_row_stride);
+        const uint4* vrow =
+            reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + r * row_elems);
+        uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(a.k_cache) + slot * row_elems);
+        uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(a.v_cache) + slot * row_elems);
+        for (int64_t i = lane; i < row_elems / E; i += 32) {
+          st_vec(kc + i, ld_vec(krow + i));
+          st_vec(vc + i, ld_vec(vrow + i));
+        }
+      }
+    }
+    if (rn >= a.tokens) break;
+#pragma unroll
+    for (int it = 0; it < P; ++it) {
+      x1v[it] = n1v[it];
+      x2v[it] = n2v[it];
+    }
+    r = rn;
+    __syncwarp();  // every lane has read cs before the next token overwrites it
   }
 }
 
 template <typename T, int PH>
 void launch_warp_rope(const RopeArgs& a, const InvFreq& freq, cudaStream_t stream) {
-  const int64_t blocks = (a.tokens + kWarpRopeWarps - 1) / kWarpRopeWarps;
+  const int64_t need = (a.tokens + kWarpRopeWarps - 1) / kWarpRopeWarps;
+  const int64_t cap = resident_blocks(reinterpret_cast<const void*>(rope_warp_kernel<T, PH>),
+                                      kWarpRopeWarps * 32, 0);
+  const int64_t blocks = need < cap ? need : cap;
   rope_warp_kernel<T, PH><<<static_cast<unsigned>(blocks), kWarpRopeWarps * 32, 0, stream>>>(a, freq);
 }
 
