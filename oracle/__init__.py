@@ -224,4 +224,15 @@ def load_reference_kernels():
     """ctypes handle of oracle/_ref/libvlref.so (the reference's CUDA kernels), or None."""
     if not REF_LIB_PATH.exists():
         return None
-    return ctypes.CDLL(str(REF_LIB_PATH))
+    lib = ctypes.CDLL(str(REF_LIB_PATH))
+    # the engine entry points (ref_harness/ref_encoder.cu) return pointers
+    lib.vlref_last_error.restype = ctypes.c_char_p
+    lib.vlref_load_weights.restype = c_void_p
+    lib.vlref_load_weights.argtypes = [ctypes.c_char_p, ctypes.c_ulonglong]
+    lib.vlref_free_weights.restype = None
+    lib.vlref_free_weights.argtypes = [c_void_p]
+    lib.vlref_weights_bytes.restype = ctypes.c_ulonglong
+    lib.vlref_weights_bytes.argtypes = [c_void_p]
+    lib.vlref_encode_batched.restype = c_int
+    lib.vlref_encode_batched.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
+    return lib

@@ -89,3 +89,50 @@ def audio_chunks_device(chunks: int, first_chunk: int, seed: int, device):
         noise.normal_(0.0, 0.01, generator=gen)
         out[i] = (x + noise).clamp_(-1.0, 1.0).float()
     return out
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """f32 -> BF16 bit patterns (uint16) by truncation (the high half of each
+    little-endian f32)."""
+    return np.ascontiguousarray(np.ascontiguousarray(x, dtype=np.float32).view(np.uint16)[..., 1::2])
+
+
+def synthetic_weights(cfg, seed: int = 0, prefixes=None) -> dict:
+    """Seeded BF16 bit patterns for every tensor of the official GLM-ASR
+    inventory of `cfg` (an AsrModelConfig), drawn uniformly with the standard
+    deviations of a usual initialisation: matrices and conv kernels
+    1/sqrt(fan_in), biases and embeddings 0.02, norm weights 1 +- 0.02, norm
+    biases 0.02.  Tensor i draws from the generator seeded with [seed, i], so
+    a subset (`prefixes`) has the same values as the full set."""
+    from .checkpoint import expected_tensors
+    out = {}
+    half_width = np.float32(np.sqrt(3.0))       # U(-a, a) has std a / sqrt(3)
+    for i, (name, shape) in enumerate(expected_tensors(cfg)):
+        if prefixes is not None and not name.startswith(tuple(prefixes)):
+            continue
+        rng = np.random.default_rng([seed, i])
+        x = rng.random(shape, dtype=np.float32)
+        x *= 2.0 * half_width
+        x -= half_width                           # unit variance
+        if "norm" in name and name.endswith(".weight"):
+            x *= np.float32(0.02)
+            x += np.float32(1.0)
+        elif name.endswith(".bias") or "embed_tokens" in name:
+            x *= np.float32(0.02)
+        else:
+            x *= np.float32(1.0 / np.sqrt(int(np.prod(shape[1:]))))
+        out[name] = bf16_bits(x)
+    return out
+
+
+def write_synthetic_checkpoint(model_dir, cfg=None, seed: int = 0):
+    """config.json + model.safetensors with synthetic_weights(cfg, seed).
+
+    The default config is GLM-ASR-Nano's audio tower and projector with a
+    one-layer, 64-token text model: the full official inventory (the
+    reference's loader accepts it), ~1.4 GB instead of ~4.5 GB."""
+    from .checkpoint import AsrModelConfig, write_checkpoint
+    if cfg is None:
+        cfg = AsrModelConfig(text_layers=1, vocab_size=64)
+    write_checkpoint(model_dir, cfg, synthetic_weights(cfg, seed))
+    return cfg
