@@ -13,6 +13,12 @@ largest configuration (configs 1-3) as a fraction of the measured HBM peak.
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Rank 0 prints one JSON line.
+
+Encoder mode (`--encoder`, one GPU): the whole GLM-ASR audio tower +
+projector (vlasr.encoder, the caller of the fused ops) on a seeded synthetic
+checkpoint, 8 chunks per step, in audio-s/s with a tensor roofline; with
+`--impl reference` the reference's own engine (run_encode_batched, compiled
+from its sources into oracle/_ref) on the same checkpoint and mel.
 """
 
 from __future__ import annotations
@@ -55,6 +61,16 @@ def parse() -> argparse.Namespace:
     p.add_argument("--gather", choices=["overlap", "blocking"], default="overlap",
                    help="all-gather each step's outputs on a side stream overlapping the "
                         "next step (default) or on the compute stream at the end of the step")
+    p.add_argument("--encoder", action="store_true",
+                   help="encoder mode: the GLM-ASR audio tower + projector (vlasr.encoder) on a "
+                        "seeded synthetic checkpoint; with --impl reference, the reference's own "
+                        "engine (run_encode_batched) on the same checkpoint and mel")
+    p.add_argument("--enc-chunks", type=int, default=8,
+                   help="chunks per encoder step (the reference engine takes at most 8)")
+    p.add_argument("--attn", default="auto", choices=["auto", "flash", "cudnn", "efficient"],
+                   help="SDPA backend of the encoder's attention")
+    p.add_argument("--gemm-acc", type=int, choices=[16, 32], default=16,
+                   help="reference encoder arm: GEMM accumulation (its default is 16)")
     p.add_argument("--op", default=None,
                    help="profiling mode: run only this op of the per-op table "
                         "(warmup + steps launches, no flush) and print its timing")
@@ -382,11 +398,156 @@ def run_reference_arm(args) -> None:
 
 
 # ---------------------------------------------------------------------------
+# encoder mode (the encoder-layer caller of the fused ops)
+# ---------------------------------------------------------------------------
+
+ENC_METRIC = "encoder audio-seconds/s (GLM-ASR audio tower + projector per 30 s chunk)"
+ENC_PARTS = ("audio_tower.", "multi_modal_projector.")
+
+
+def _event_time(fn, steps: int, warmup: int, stream) -> float:
+    """ms per call, CUDA events on `stream` around `steps` queued calls."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_encoder_bench(args) -> None:
+    """One GPU: the encoder pass over `--enc-chunks` chunks per step.
+
+    Both arms read the same seeded synthetic checkpoint (the full official
+    inventory, written to a temporary directory) and the same mel
+    (vlasr.logmel of seeded audio).  Ours keeps mel on the device for `value`;
+    `e2e` adds the pinned-host mel upload and the projector download.  The
+    reference arm calls its run_encode_batched (host mel in, device FP16
+    projector out, synchronous), compiled from its sources into oracle/_ref."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import shutil
+    import tempfile
+
+    import torch
+    import vlasr
+    from vlasr.checkpoint import load_weights
+    from vlasr.encoder import AudioEncoder, flops_per_chunk
+    from vlasr.synth import audio_chunks_device, write_synthetic_checkpoint
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    vlasr.load()
+    chunks = args.enc_chunks
+    ckpt = tempfile.mkdtemp(prefix="vl_glmasr_")
+    try:
+        write_synthetic_checkpoint(ckpt, seed=11)
+        mel = vlasr.logmel(audio_chunks_device(chunks, 0, 5, dev))
+        stream = torch.cuda.current_stream(dev)
+        base = {"metric": ENC_METRIC, "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "data": "synthetic (seeded audio -> vlasr.logmel; seeded "
+                "synthetic checkpoint with the official GLM-ASR inventory)"}
+        sampler = ClockSampler(0)
+        if args.impl == "reference":
+            import ctypes
+
+            import numpy as np
+            import oracle
+            lib = oracle.load_reference_kernels()
+            if lib is None:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "oracle/_ref/libvlref.so not built"}), flush=True)
+                return
+            handle = lib.vlref_load_weights(ckpt.encode(), 64 << 30)
+            if not handle:
+                raise SystemExit(lib.vlref_last_error().decode())
+            mel_host = np.ascontiguousarray(mel.cpu().numpy())
+            out = torch.empty(chunks * 375, 2048, dtype=torch.float16, device=dev)
+
+            def call():
+                rc = lib.vlref_encode_batched(handle, mel_host.ctypes.data_as(ctypes.c_void_p),
+                                              chunks, int(args.gemm_acc == 16),
+                                              ctypes.c_void_p(out.data_ptr()))
+                if rc:
+                    raise SystemExit(lib.vlref_last_error().decode())
+
+            sampler.start()
+            ms = _event_time(call, args.steps, args.warmup, stream)
+            clocks = sampler.stop()
+            lib.vlref_free_weights(handle)
+            value = chunks * AUDIO_SECONDS_PER_CHUNK / (ms / 1e3)
+            line = {"impl": "reference", **base, "value": round(value, 1),
+                    "ms_per_step": round(ms, 3), "dtype": "fp16",
+                    "config": {"workload": "encoder", "chunks_per_step": chunks, "layers": 32,
+                               "gemm_acc": f"fp{args.gemm_acc}",
+                               "api": "run_encode_batched (host f32 mel in, device FP16 "
+                                      "projector out, synchronous)"},
+                    "e2e": {"value": round(value, 1), "unit": "audio-s/s",
+                            "h2d_bytes_per_step": mel_host.size * 2, "d2h_bytes_per_step": 0},
+                    "clocks": clocks}
+            print(json.dumps(line), flush=True)
+            return
+
+        _, w = load_weights(ckpt, dev, prefixes=ENC_PARTS)
+        enc = AudioEncoder(w, dtype=torch.bfloat16, attention=args.attn)
+        sampler.start()
+        time.sleep(0.3)
+        ms = _event_time(lambda: enc.encode(mel), args.steps, args.warmup, stream)
+        clocks = sampler.stop()
+        flops = flops_per_chunk(enc.shape) * chunks
+        tflops = flops / (ms * 1e-3) / 1e12
+        try:
+            pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+            peak, peak_kind = float(pk["bf16_tflops_sustained"]), "measured (sustained)"
+        except Exception:  # noqa: BLE001
+            peak, peak_kind = 1400.0, "fallback (sustained)"
+        # e2e: pinned host mel -> device, encode, projector -> pinned host
+        mel_host = mel.cpu().pin_memory()
+        mel_dev = torch.empty_like(mel)
+        proj_host = torch.empty((chunks * 375, 2048), dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            mel_dev.copy_(mel_host, non_blocking=True)
+            proj_host.copy_(enc.encode(mel_dev), non_blocking=True)
+
+        e_ms = _event_time(e2e_step, args.steps, args.warmup, stream)
+        value = chunks * AUDIO_SECONDS_PER_CHUNK / (ms / 1e3)
+        line = {**base, "value": round(value, 1), "ms_per_step": round(ms, 3), "dtype": "bf16",
+                "config": {"workload": "encoder", "chunks_per_step": chunks, "layers": 32,
+                           "gemm_acc": "fp32", "attention": f"torch SDPA ({args.attn})",
+                           "flops_per_step": flops,
+                           "l2": "activations of 8 chunks (>= 30 MB per tensor) and 1.3 GB of "
+                                 "weights stream through L2 every step"},
+                "roofline": {"bound": "tensor", "kernel": "whole encoder pass (cuBLAS GEMMs, "
+                             "SDPA, vlasr fused ops)", "achieved": round(tflops, 1),
+                             "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                             "frac": round(tflops / peak, 4), "traffic": None},
+                "e2e": {"value": round(chunks * AUDIO_SECONDS_PER_CHUNK / (e_ms / 1e3), 1),
+                        "unit": "audio-s/s", "ms_per_step": round(e_ms, 3),
+                        "h2d_bytes_per_step": mel_host.numel() * 4,
+                        "d2h_bytes_per_step": proj_host.numel() * 2,
+                        "api": "vlasr.encoder.AudioEncoder.encode"},
+                "gpu_launches": enc.launches_per_pass() * args.steps, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    finally:
+        shutil.rmtree(ckpt, ignore_errors=True)
+
+
+# ---------------------------------------------------------------------------
 # main arm
 # ---------------------------------------------------------------------------
 
 def main() -> None:
     args = parse()
+    if args.encoder:
+        run_encoder_bench(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
         return

@@ -322,7 +322,8 @@ def load_weights(model_dir: str | os.PathLike, device, dtype=None, prefixes=None
         slots.append(cursor)
         cursor += (t.nbytes + ARENA_ALIGN - 1) // ARENA_ALIGN * ARENA_ALIGN
     dev = torch.device(device)
-    arena = torch.empty(max(cursor, ARENA_ALIGN), dtype=torch.uint8, device=dev)
+    raw = torch.empty(cursor + ARENA_ALIGN, dtype=torch.uint8, device=dev)
+    arena = raw[(-raw.data_ptr()) % ARENA_ALIGN:]          # 256-byte aligned base
     lo = min((t.begin for t in tensors), default=0)
     hi = max((t.end for t in tensors), default=0)
     mm = np.memmap(Path(model_dir) / "model.safetensors", dtype=np.uint8, mode="r",

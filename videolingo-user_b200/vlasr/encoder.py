@@ -28,6 +28,7 @@ from one GEMM instead of three.
 
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 
 import torch
@@ -72,6 +73,21 @@ def _shape_from(weights: dict, heads: int) -> EncoderShape:
         rotary_dim=head_dim // 2)       # partial_rotary_factor 0.5
 
 
+def flops_per_chunk(s: EncoderShape, mel_frames: int = 3000) -> int:
+    """Multiply-add FLOPs (2 per MAC) of one chunk: conv frontend, per layer
+    the q/k/v/o and MLP GEMMs plus q k^T and p v, and the projector."""
+    frames = (mel_frames - 1) // 2 + 1
+    conv = 2 * mel_frames * s.hidden * s.mel_bins * 3 + 2 * frames * s.hidden * s.hidden * 3
+    layer = (2 * frames * (4 * s.hidden * s.hidden + 2 * s.hidden * s.ffn)
+             + 2 * 2 * s.heads * frames * frames * s.head_dim)
+    proj = 2 * (frames // MERGE) * (MERGE * s.hidden * s.proj_mid + s.proj_mid * s.out_dim)
+    return conv + s.layers * layer + proj
+
+
+_SDPA = {"flash": "FLASH_ATTENTION", "cudnn": "CUDNN_ATTENTION",
+         "efficient": "EFFICIENT_ATTENTION", "math": "MATH"}
+
+
 class AudioEncoder:
     """Resident weights in one compute dtype (bf16 or fp16) and the launch
     sequence of the audio tower + projector.
@@ -82,10 +98,13 @@ class AudioEncoder:
     (tests).  Buffers are allocated per chunk count and reused."""
 
     def __init__(self, weights: dict, *, heads: int = 20, dtype=torch.bfloat16,
-                 layers: int | None = None):
+                 layers: int | None = None, attention: str = "auto"):
         if dtype not in (torch.bfloat16, torch.float16):
             raise VlasrInputError("AudioEncoder computes in bf16 or fp16")
+        if attention != "auto" and attention not in _SDPA:
+            raise VlasrInputError(f"attention must be 'auto' or one of {sorted(_SDPA)}")
         self.dtype = dtype
+        self.attention = attention
         s = _shape_from(weights, heads)
         if layers is not None:
             if not 0 <= layers <= s.layers:
@@ -178,6 +197,12 @@ class AudioEncoder:
         h, y, qkv, o, f = b["h"], b["y"], b["qkv"], b["o"], b["f"]
         hs, nh, hd = s.hidden, s.heads, s.head_dim
         out = {}
+        if self.attention == "auto":
+            sdpa_ctx = contextlib.nullcontext
+        else:
+            from torch.nn.attention import SDPBackend, sdpa_kernel
+            backend = getattr(SDPBackend, _SDPA[self.attention])
+            sdpa_ctx = lambda: sdpa_kernel([backend])  # noqa: E731
         self.conv_frontend(mel, h)
         if stages:
             out["conv_hidden"] = h.clone()
@@ -189,7 +214,8 @@ class AudioEncoder:
                       base=s.rope_base, seq_len=frames)
             q, k, v = (qkv[:, i * hs:(i + 1) * hs].view(chunks, frames, nh, hd).transpose(1, 2)
                        for i in range(3))
-            a = F.scaled_dot_product_attention(q, k, v)           # [C, heads, frames, hd]
+            with sdpa_ctx():
+                a = F.scaled_dot_product_attention(q, k, v)       # [C, heads, frames, hd]
             a = a.transpose(1, 2).reshape(chunks * frames, hs)
             torch.addmm(lw["o_b"], a, lw["o_wt"], out=o)
             ops.add_layernorm(h, o, lw["ln2_w"], lw["ln2_b"], eps=s.eps, out=y)
