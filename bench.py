@@ -311,6 +311,31 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
                 lambda: vlasr.rope_kv_append(q, k, v, kc, vc, pos32, slots, head_dim=128,
                                              rotary_dim=64))
 
+    def _attn_bytes(q, pos, fused):
+        # K and V rows of positions 0..p per (token, kv head) + q in + out;
+        # fused: + new k/v rows in and the appended cache rows out
+        kv_rows = int((pos.long() + 1).sum())
+        b = kv_rows * 2 * 4 * 128 * 2 + 2 * q.numel() * 2
+        return b + (4 * 64 * 4 * 128 * 2 if fused else 0)
+
+    def decode_attention():
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        start = slots - pos32.long()
+        out = torch.empty(64, 16 * 128, dtype=bf, device=dev)
+        return ("q [64,16,128] over K/V caches 64 x 4096 slots x [4,128], pos U[0,4096)",
+                _attn_bytes(q, pos32, False),
+                lambda: vlasr.decode_attention(q, kc, vc, pos32, start, n_kv_heads=4,
+                                               head_dim=128, max_seq_len=4096, out=out))
+
+    def decode_step_fused():
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        start = slots - pos32.long()
+        out = torch.empty(64, 16 * 128, dtype=bf, device=dev)
+        return ("RoPE(q,k) + KV append + attention, config 3", _attn_bytes(q, pos32, True),
+                lambda: vlasr.decode_attention(q, kc, vc, pos32, start, n_kv_heads=4,
+                                               head_dim=128, max_seq_len=4096, k=k, v=v,
+                                               rotary_dim=128, out=out))
+
     table = [  # name, builder, iterations, latency-bound
         ("add_layernorm", add_layernorm, 20, False),
         ("gelu_erf", gelu_erf, 20, False),
@@ -324,6 +349,8 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         ("decode_rope", decode_rope, 20, True),
         ("decode_kv_append", decode_kv_append, 20, True),
         ("decode_rope_kv_append", decode_rope_kv_append, 20, True),
+        ("decode_attention", decode_attention, 20, False),
+        ("decode_step_fused", decode_step_fused, 20, False),
     ]
     rows = {}
     for name, build, iters, latency in table:

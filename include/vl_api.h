@@ -294,6 +294,54 @@ VL_EXPORT int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache,
                       int rotary_dim, double base, int64_t num_slots,
                       int dtype, int32_t* status, void* stream);
 
+/*
+ * Decode-step attention: one query token per sequence against its KV cache,
+ * grouped-query heads (n_q_heads / n_kv_heads query heads share a kv head),
+ * optionally fused with the RoPE of q and k at the token's position and the
+ * append of the new k / v rows.  One launch replaces the reference's
+ * rope_at_position_map_kernel + append_kv_mapped_kernel +
+ * attention_step_mapped_kernel (native/asr/src/decoder.cu:471-572, launched
+ * at :1710-1722), without its 1024-position limit.
+ *
+ * Token t (query row q + t*q_row_stride, [n_q_heads][head_dim]) sits at
+ * position p = positions[t] of a sequence whose cache rows are the slots
+ * seq_start[t] + 0 .. seq_start[t] + p of k_cache / v_cache
+ * ([num_slots][cache_row_stride] elements, kv head h at h*head_dim).
+ * out row t = softmax(scale * q . K^T) V over positions 0..p (scale 0 means
+ * 1/sqrt(head_dim)), per query head, fp32 arithmetic, rounded once.
+ *
+ * With k and v given (rows k/v + t*kv_row_stride, [n_kv_heads][head_dim]),
+ * q and k are first rotated at p (rotate-half over the first rotary_dim
+ * dims, base rope_base; rotary_dim 0 = no RoPE), and the rotated k and the v
+ * row are stored to slot seq_start[t] + p; the inputs are not modified.
+ * With k = v = NULL the cache must already hold position p.
+ *
+ * A token with p outside [0, max_seq_len) or a slot outside [0, num_slots)
+ * gets zero output and sets VL_STATUS_BAD_SLOT in *status (if given).
+ * Supported: f16 / bf16; head_dim 64 or 128 with 1, 2, 4 or 8 query heads
+ * per kv head; max_seq_len <= VL_DECODE_MAX_SEQ_LEN.  One call must not
+ * read a slot that another token of the same call appends (one token per
+ * sequence per call, as in a decode step).
+ * workspace: vl_decode_attention_workspace_bytes(...) bytes, zero-filled
+ * before its first use; every call leaves it zero-filled again (the split
+ * counters reset themselves), so one workspace serves calls in stream order.
+ */
+#define VL_DECODE_MAX_SEQ_LEN 262144
+
+VL_EXPORT size_t vl_decode_attention_workspace_bytes(int64_t tokens, int n_q_heads,
+                                                     int n_kv_heads, int head_dim,
+                                                     int64_t max_seq_len);
+
+VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
+                                  void* k_cache, void* v_cache, const int32_t* positions,
+                                  const int64_t* seq_start, int64_t tokens, int n_q_heads,
+                                  int n_kv_heads, int head_dim, int rotary_dim,
+                                  double rope_base, float scale, int64_t q_row_stride,
+                                  int64_t kv_row_stride, int64_t cache_row_stride,
+                                  int64_t max_seq_len, int64_t num_slots, void* out,
+                                  int64_t out_row_stride, int dtype, void* workspace,
+                                  size_t workspace_bytes, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -53,10 +53,14 @@ def _load():
         lib.or_swiglu.argtypes = [fp, fp, fp, c_int64, c_int]
         lib.or_rope.argtypes = [fp, fp, POINTER(c_int64), c_int64, c_int, c_int, c_int, c_int,
                                 c_double, c_int]
+        lib.or_decode_attention.argtypes = [fp, c_void_p, c_void_p, fp, fp, POINTER(ctypes.c_int32),
+                                            POINTER(c_int64), c_int64, c_int, c_int, c_int,
+                                            c_int, c_double, c_float, c_int, fp]
         lib.or_mel_filterbank.argtypes = [POINTER(c_double)]
         lib.or_logmel_ref.argtypes = [fp, c_int64, fp]
         for name in ("or_round_array", "or_add_layernorm", "or_add_rmsnorm", "or_gelu",
-                     "or_swiglu", "or_rope", "or_mel_filterbank", "or_logmel_ref"):
+                     "or_swiglu", "or_rope", "or_mel_filterbank", "or_logmel_ref",
+                     "or_decode_attention"):
             getattr(lib, name).restype = None
         _lib = lib
     return _lib
@@ -133,6 +137,31 @@ def rope(q, k, positions, head_dim: int, rotary_dim: int, base: float, dtype: st
     _load().or_rope(_fp(qq), _fp(kk), pos.ctypes.data_as(POINTER(c_int64)), tokens,
                     qq.shape[1], kk.shape[1], head_dim, rotary_dim, base, DTYPE_CODES[dtype])
     return qq, (kk if k is not None else None)
+
+
+def decode_attention(q, k_cache, v_cache, positions, seq_start, *, k=None, v=None,
+                     rotary_dim: int = 0, base: float = 10000.0, scale: float | None = None,
+                     dtype: str = "bf16"):
+    """Decode step: q [tokens, nq, hd]; caches [num_slots, nkv, hd] (copies are
+    updated with the new rows when k/v are given).  Returns (out [tokens, nq,
+    hd], k_cache', v_cache')."""
+    qq = _f32(q).copy()
+    tokens, nq, hd = qq.shape
+    kc = _f32(k_cache).copy()
+    vc = _f32(v_cache).copy()
+    nkv = kc.shape[1]
+    kk = _f32(k).copy() if k is not None else None
+    vv = _f32(v).copy() if v is not None else None
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    st = np.ascontiguousarray(seq_start, dtype=np.int64)
+    out = np.empty((tokens, nq, hd), dtype=np.float32)
+    sc = float(1.0 / np.sqrt(hd)) if scale is None else float(scale)
+    _load().or_decode_attention(
+        _fp(qq), None if kk is None else kk.ctypes.data_as(c_void_p),
+        None if vv is None else vv.ctypes.data_as(c_void_p), _fp(kc), _fp(vc),
+        pos.ctypes.data_as(POINTER(ctypes.c_int32)), st.ctypes.data_as(POINTER(c_int64)),
+        tokens, nq, nkv, hd, rotary_dim, base, sc, DTYPE_CODES[dtype], _fp(out))
+    return out, kc, vc
 
 
 def mel_filterbank_f64() -> np.ndarray:

@@ -102,4 +102,16 @@ int vlref_append_kv_mapped(const void* k, const void* v, void* k_cache, void* v_
   return static_cast<int>(cudaGetLastError());
 }
 
+// Decode attention (decoder.cu:1719-1722 launch shape): cache layout
+// [chunk][layer][K|V][1024][512]; row r attends chunk active[r] over positions
+// 0..positions[active[r]] (< 1024); q / out [rows][2048].
+int vlref_attention_mapped(const void* q, const void* kv_cache, void* out, const int* positions,
+                           const int* active, int rows, int layer,
+                           unsigned long long layer_stride, unsigned long long chunk_stride) {
+  attention_step_mapped_kernel<<<rows * kTextHeads, 128, (kMaxSequence + 128) * sizeof(float)>>>(
+      static_cast<const half*>(q), static_cast<const half*>(kv_cache), static_cast<half*>(out),
+      positions, active, rows, layer, layer_stride, chunk_stride);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // extern "C"

@@ -276,3 +276,67 @@ void or_logmel_ref(const float* pcm, int64_t chunks, float* out) {
   free(power);
   free(frame);
 }
+
+/* ------------------------------------------------------------------------ */
+/* Decode step (decoder.cu:471-572, launched at :1710-1722)                  */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * rope_at_position_map_kernel + append_kv_mapped_kernel +
+ * attention_step_mapped_kernel for `tokens` rows.  q [tokens][nq*hd],
+ * k_new / v_new [tokens][nkv*hd] (NULL: the cache already holds position p),
+ * caches [num_slots][nkv*hd].  Token t at position p = positions[t] uses
+ * cache slots seq_start[t] + 0..p.  With rot > 0 q and k_new are rotated at
+ * p (fp64 angle, fp32 cos/sin, results rounded to the storage type, as the
+ * reference stores them), k_new / v_new are written to slot seq_start[t]+p.
+ * Scores dot*scale (fp32, dims in order), softmax with max, expf and the sum
+ * in position order, normalised probabilities, out = sum_t p_t v_t in
+ * position order, rounded once.  q_new / k_new are modified (rotated).
+ */
+void or_decode_attention(float* q, float* k_new, const float* v_new, float* k_cache,
+                         float* v_cache, const int32_t* positions, const int64_t* seq_start,
+                         int64_t tokens, int nq, int nkv, int hd, int rot, double base,
+                         float scale, int dtype, float* out) {
+  const int group = nq / nkv;
+  const int64_t row = (int64_t)nkv * hd;
+  for (int64_t t = 0; t < tokens; ++t) {
+    const int64_t p = positions[t];
+    float* qt = q + t * (int64_t)nq * hd;
+    if (k_new != NULL) {
+      float* kt = k_new + t * row;
+      if (rot > 0) {
+        const int64_t pos64 = p;
+        or_rope(qt, kt, &pos64, 1, nq, nkv, hd, rot, base, dtype);
+      }
+      memcpy(k_cache + (seq_start[t] + p) * row, kt, (size_t)row * sizeof(float));
+      memcpy(v_cache + (seq_start[t] + p) * row, v_new + t * row, (size_t)row * sizeof(float));
+    }
+    float* scores = (float*)malloc((size_t)(p + 1) * sizeof(float));
+    for (int h = 0; h < nq; ++h) {
+      const int kvh = h / group;
+      const float* qh = qt + (int64_t)h * hd;
+      float mx = -INFINITY;
+      for (int64_t s = 0; s <= p; ++s) {
+        const float* kr = k_cache + (seq_start[t] + s) * row + (int64_t)kvh * hd;
+        float dot = 0.0f;
+        for (int d = 0; d < hd; ++d) dot = fmaf(qh[d], kr[d], dot);
+        scores[s] = dot * scale;
+        if (scores[s] > mx) mx = scores[s];
+      }
+      float total = 0.0f;
+      for (int64_t s = 0; s <= p; ++s) {
+        scores[s] = expf(scores[s] - mx);
+        total += scores[s];
+      }
+      const float inv = 1.0f / total;
+      for (int64_t s = 0; s <= p; ++s) scores[s] *= inv;
+      for (int d = 0; d < hd; ++d) {
+        float acc = 0.0f;
+        for (int64_t s = 0; s <= p; ++s)
+          acc = fmaf(scores[s], v_cache[(seq_start[t] + s) * row + (int64_t)kvh * hd + d], acc);
+        out[(t * nq + h) * (int64_t)hd + d] = or_round(dtype, acc);
+      }
+    }
+    free(scores);
+  }
+}

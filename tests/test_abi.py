@@ -30,6 +30,7 @@ def test_header_declares_the_expected_ops():
     syms = declared_symbols()
     for name in ("vl_logmel", "vl_add_layernorm", "vl_add_rmsnorm", "vl_gelu_erf", "vl_swiglu",
                  "vl_rope_inplace", "vl_embed_gather", "vl_kv_append", "vl_rope_kv_append",
+                 "vl_decode_attention", "vl_decode_attention_workspace_bytes",
                  "vl_last_error", "vl_logmel_workspace_bytes"):
         assert name in syms
 
@@ -135,6 +136,36 @@ def test_index_ops_reject(lib):
                             None) == 2
     assert lib.vl_rope_kv_append(FAKE, FAKE * 2, None, FAKE, FAKE, FAKE, FAKE, 4, 16, 4, 128, 64,
                                  10000.0, 64, 2, None, None) == 2
+
+
+def test_decode_attention_rejects(lib):
+    def call(q=FAKE, k=None, v=None, kc=FAKE * 2, vc=FAKE * 3, pos=FAKE * 4, st=FAKE * 5,
+             tokens=4, nq=16, nkv=4, hd=128, rot=0, base=10000.0, scale=0.0, qs=2048, ks=512,
+             cs=512, max_len=1024, slots=4096, out=FAKE * 6, os_=2048, dtype=2, ws=FAKE * 7,
+             ws_bytes=1 << 30):
+        return lib.vl_decode_attention(q, k, v, kc, vc, pos, st, tokens, nq, nkv, hd, rot, base,
+                                       scale, qs, ks, cs, max_len, slots, out, os_, dtype, ws,
+                                       ws_bytes, None, None)
+
+    assert call(q=None) == 2 and "null" in _err(lib)
+    assert call(k=FAKE * 8) == 2 and "both" in _err(lib)
+    assert call(dtype=0) == 2 and "dtype" in _err(lib)
+    assert call(nq=14) == 2 and "shape" in _err(lib)
+    assert call(hd=96) == 2 and "head_dim" in _err(lib)
+    assert call(nq=64, qs=8192, os_=8192) == 2 and "group" in _err(lib)  # 16 per kv head
+    assert call(rot=64) == 2 and "RoPE" in _err(lib)            # rotation needs the new k
+    assert call(rot=3, k=FAKE * 8, v=FAKE * 9) == 2 and "rotary_dim" in _err(lib)
+    assert call(max_len=0) == 2 and "max_seq_len" in _err(lib)
+    assert call(max_len=(1 << 18) + 1) == 2
+    assert call(cs=256) == 2 and "stride" in _err(lib)
+    assert call(qs=2052) == 2 and "multiples of 8" in _err(lib)
+    assert call(q=FAKE + 4) == 2 and "aligned" in _err(lib)
+    assert call(ws_bytes=16) == 2 and "workspace" in _err(lib)
+    assert call(out=FAKE * 2) == 2 and "overlaps" in _err(lib)
+    assert call(scale=float("nan")) == 2 and "scale" in _err(lib)
+    assert lib.vl_decode_attention_workspace_bytes(64, 16, 4, 128, 4096) >= 64 * 4 * 4
+    assert lib.vl_decode_attention_workspace_bytes(0, 16, 4, 128, 4096) == 0
+    assert lib.vl_decode_attention_workspace_bytes(1, 16, 3, 128, 4096) == 0
 
 
 def test_error_is_thread_local(lib):

@@ -373,4 +373,96 @@ int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache, void* v_ca
                      "vl_rope_kv_append");
 }
 
+size_t vl_decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_heads,
+                                           int head_dim, int64_t max_seq_len) {
+  if (tokens <= 0 || n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads != 0 ||
+      head_dim <= 0 || max_seq_len <= 0 || max_seq_len > VL_DECODE_MAX_SEQ_LEN ||
+      tokens > kMaxRows)
+    return 0;
+  return vl::decode_attention_workspace_bytes(tokens, n_q_heads, n_kv_heads, head_dim,
+                                              max_seq_len);
+}
+
+int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cache,
+                        void* v_cache, const int32_t* positions, const int64_t* seq_start,
+                        int64_t tokens, int n_q_heads, int n_kv_heads, int head_dim,
+                        int rotary_dim, double rope_base, float scale, int64_t q_row_stride,
+                        int64_t kv_row_stride, int64_t cache_row_stride, int64_t max_seq_len,
+                        int64_t num_slots, void* out, int64_t out_row_stride, int dtype,
+                        void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  const char* op = "vl_decode_attention";
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || positions == nullptr ||
+      seq_start == nullptr || out == nullptr)
+    return fail(VL_ERR_INVALID, "%s: null pointer", op);
+  if ((k == nullptr) != (v == nullptr))
+    return fail(VL_ERR_INVALID, "%s: k and v must both be given or both be null", op);
+  if (dtype != VL_F16 && dtype != VL_BF16)
+    return fail(VL_ERR_INVALID, "%s: unsupported dtype %d (f16 or bf16)", op, dtype);
+  if (tokens < 0 || tokens > 0x7fffffff || n_q_heads <= 0 || n_kv_heads <= 0 ||
+      n_kv_heads > 65535 || n_q_heads % n_kv_heads != 0)
+    return fail(VL_ERR_INVALID, "%s: bad shape tokens=%lld heads=%d/%d", op,
+                static_cast<long long>(tokens), n_q_heads, n_kv_heads);
+  if (!vl::decode_attention_supported(head_dim, n_q_heads / n_kv_heads))
+    return fail(VL_ERR_INVALID,
+                "%s: unsupported head_dim %d / group %d (head_dim 64 or 128 with 1, 2, 4 or 8 "
+                "query heads per kv head)", op, head_dim,
+                n_q_heads / n_kv_heads);
+  if (rotary_dim < 0 || rotary_dim % 2 != 0 || rotary_dim > head_dim)
+    return fail(VL_ERR_INVALID, "%s: rotary_dim must be even, in [0, head_dim]", op);
+  if (rotary_dim > 0 && k == nullptr)
+    return fail(VL_ERR_INVALID, "%s: RoPE needs the new k row (k is null)", op);
+  if (rotary_dim > 0 && (!(rope_base > 0.0) || !std::isfinite(rope_base)))
+    return fail(VL_ERR_INVALID, "%s: rope_base must be finite and > 0", op);
+  if (!std::isfinite(scale) || scale < 0.0f)
+    return fail(VL_ERR_INVALID, "%s: scale must be finite and >= 0", op);
+  if (max_seq_len <= 0 || max_seq_len > VL_DECODE_MAX_SEQ_LEN || num_slots < 0)
+    return fail(VL_ERR_INVALID, "%s: max_seq_len must be in [1, %d], num_slots >= 0", op,
+                VL_DECODE_MAX_SEQ_LEN);
+  const int64_t qw = static_cast<int64_t>(n_q_heads) * head_dim;
+  const int64_t kw = static_cast<int64_t>(n_kv_heads) * head_dim;
+  if (q_row_stride < qw || out_row_stride < qw || cache_row_stride < kw ||
+      (k != nullptr && kv_row_stride < kw))
+    return fail(VL_ERR_INVALID, "%s: row strides must cover heads * head_dim", op);
+  if (q_row_stride % 8 || out_row_stride % 8 || cache_row_stride % 8 ||
+      (k != nullptr && kv_row_stride % 8))
+    return fail(VL_ERR_INVALID, "%s: row strides must be multiples of 8 elements", op);
+  if (!vl::aligned16(q) || !vl::aligned16(k_cache) || !vl::aligned16(v_cache) ||
+      !vl::aligned16(out) || (k != nullptr && (!vl::aligned16(k) || !vl::aligned16(v))))
+    return fail(VL_ERR_INVALID, "%s: q, k, v, caches and out must be 16-byte aligned", op);
+  if (tokens == 0) return ok();
+  const size_t need = vl::decode_attention_workspace_bytes(tokens, n_q_heads, n_kv_heads,
+                                                           head_dim, max_seq_len);
+  if (workspace == nullptr || workspace_bytes < need || !vl::aligned16(workspace))
+    return fail(VL_ERR_INVALID, "%s: workspace of %zu bytes (16-byte aligned) required", op,
+                need);
+  if (overlaps(out, tokens * out_row_stride * 2, k_cache, num_slots * cache_row_stride * 2) ||
+      overlaps(out, tokens * out_row_stride * 2, v_cache, num_slots * cache_row_stride * 2))
+    return fail(VL_ERR_INVALID, "%s: out overlaps a cache", op);
+  vl::DecodeAttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.positions = positions;
+  a.seq_start = seq_start;
+  a.out = out;
+  a.tokens = tokens;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.rope_base = rope_base;
+  a.scale = scale > 0.0f ? scale : 1.0f / std::sqrt(static_cast<float>(head_dim));
+  a.q_row_stride = q_row_stride;
+  a.kv_row_stride = kv_row_stride;
+  a.cache_row_stride = cache_row_stride;
+  a.out_row_stride = out_row_stride;
+  a.max_seq_len = max_seq_len;
+  a.num_slots = num_slots;
+  a.status = status;
+  return exec_status(
+      vl::launch_decode_attention(a, dtype, workspace, static_cast<cudaStream_t>(stream)), op);
+}
+
 }  // extern "C"

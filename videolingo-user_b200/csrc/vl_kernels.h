@@ -58,6 +58,44 @@ cudaError_t launch_kv_append(const void* k, const void* v, void* k_cache, void* 
                              int64_t k_row_stride_bytes, int64_t v_row_stride_bytes,
                              int64_t num_slots, int32_t* status, cudaStream_t stream);
 
+// Decode-step attention (vl_attn.cu).
+struct DecodeAttnArgs {
+  const void* q;            // [tokens][n_q_heads * head_dim], row stride q_row_stride
+  const void* k;            // new rows [tokens][n_kv_heads * head_dim] or nullptr
+  const void* v;
+  void* k_cache;            // [num_slots][cache_row_stride]
+  void* v_cache;
+  const int32_t* positions; // [tokens]
+  const int64_t* seq_start; // [tokens] slot of position 0
+  void* out;                // [tokens][n_q_heads * head_dim], row stride out_row_stride
+  int64_t tokens;
+  int n_q_heads;
+  int n_kv_heads;
+  int head_dim;
+  int rotary_dim;           // 0: no RoPE
+  double rope_base;
+  float scale;
+  int64_t q_row_stride;
+  int64_t kv_row_stride;
+  int64_t cache_row_stride;
+  int64_t out_row_stride;
+  int64_t max_seq_len;
+  int64_t num_slots;
+  int32_t* status;
+  // filled by launch_decode_attention
+  int split;
+  int max_splits;
+  int* counters;
+  float* o_part;
+  float2* ml_part;
+};
+bool decode_attention_supported(int head_dim, int group);
+int64_t decode_attention_split(int64_t tokens, int n_kv_heads, int64_t max_seq_len);
+size_t decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_heads,
+                                        int head_dim, int64_t max_seq_len);
+cudaError_t launch_decode_attention(DecodeAttnArgs args, int dtype, void* workspace,
+                                    cudaStream_t stream);
+
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream);

@@ -22,34 +22,13 @@
 
 #include "vl_common.cuh"
 #include "vl_kernels.h"
+#include "vl_rope_math.cuh"
 
 namespace vl {
 namespace {
 
 constexpr int kRopeThreads = 128;
-constexpr int kMaxHalfRot = 128;
 constexpr int kMaxTokensPerBlock = 8;
-
-struct InvFreq {
-  double v[kMaxHalfRot];
-};
-
-// cos/sin of angle = pos * inv_freq (formed in fp64, as the reference's host
-// tables are): the angle is reduced modulo 2*pi in fp64 (Cody-Waite with a
-// two-term 2*pi), then evaluated with fp32 sincosf on [-pi, pi].  Against
-// rounding fp64 cos/sin to fp32 the difference is below 3e-7 absolute, at a
-// fraction of the cost of an fp64 sincos.
-__device__ __forceinline__ float2 rope_cos_sin(double angle) {
-  constexpr double kTwoPiHi = 6.283185307179586232;        // 2*pi rounded to double
-  constexpr double kTwoPiLo = 2.4492935982947064e-16;      // 2*pi - kTwoPiHi
-  constexpr double kInvTwoPi = 0.15915494309189533577;
-  const double k = rint(angle * kInvTwoPi);
-  double r = fma(-k, kTwoPiHi, angle);
-  r = fma(-k, kTwoPiLo, r);
-  float sn, cs;
-  sincosf(static_cast<float>(r), &sn, &cs);
-  return make_float2(cs, sn);
-}
 
 __device__ __forceinline__ int64_t token_position(const RopeArgs& a, int64_t r) {
   if (a.positions == nullptr) return a.pos_offset + (a.seq_len > 0 ? r % a.seq_len : r);
@@ -323,9 +302,7 @@ template <typename T>
 cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
   constexpr int E = Storage<T>::kVec;
   const int half_rot = a.rotary_dim / 2;
-  InvFreq freq;
-  for (int d = 0; d < half_rot; ++d)
-    freq.v[d] = 1.0 / std::pow(a.base, static_cast<double>(2 * d) / a.rotary_dim);
+  const InvFreq freq = make_inv_freq(a.base, a.rotary_dim);
   const int64_t row_elems = static_cast<int64_t>(a.n_k_heads) * a.head_dim;
   bool vec = half_rot % E == 0 && a.head_dim % E == 0 && aligned16(a.q) &&
              a.q_row_stride % E == 0 &&

@@ -284,6 +284,119 @@ def rope_kv_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: t
 
 
 # ---------------------------------------------------------------------------
+# Decode-step attention
+# ---------------------------------------------------------------------------
+
+def decode_attention_workspace_bytes(tokens: int, n_q_heads: int, n_kv_heads: int,
+                                     head_dim: int, max_seq_len: int) -> int:
+    return int(_lib.load().vl_decode_attention_workspace_bytes(tokens, n_q_heads, n_kv_heads,
+                                                               head_dim, max_seq_len))
+
+
+_attn_ws: dict = {}
+
+
+def _attn_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A zero-filled workspace per device, grown on demand (calls in stream
+    order leave it zero-filled)."""
+    key = (device.type, device.index)
+    ws = _attn_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _attn_ws[key] = ws
+    return ws
+
+
+def _rows_of(t: torch.Tensor, width: int, name: str) -> tuple[int, int]:
+    """(rows, row stride) of t viewed as rows of `width` contiguous elements."""
+    _cuda(t, name)
+    if t.stride(-1) != 1:
+        raise VlasrInputError(f"{name} must have a contiguous last dim")
+    if t.dim() >= 3:
+        inner = t.shape[-1] * t.shape[-2]
+        if inner != width or t.stride(-2) != t.shape[-1]:
+            raise VlasrInputError(f"{name} rows must be [heads, head_dim] packed ({width} elements)")
+        lead = t.shape[:-2]
+        stride = t.stride(-3)
+    else:
+        if t.shape[-1] != width:
+            raise VlasrInputError(f"{name} rows must have {width} elements")
+        lead = t.shape[:-1]
+        stride = t.stride(-2) if t.dim() == 2 else width
+    rows = 1
+    for d in lead:
+        rows *= d
+    if len(lead) > 1 and not t.is_contiguous():
+        raise VlasrInputError(f"{name} leading dims must be contiguous")
+    return rows, stride
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     positions: torch.Tensor, seq_start: torch.Tensor, *, n_kv_heads: int,
+                     head_dim: int, max_seq_len: int, k: torch.Tensor | None = None,
+                     v: torch.Tensor | None = None, rotary_dim: int = 0,
+                     rope_base: float = 10000.0, scale: float = 0.0,
+                     out: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None,
+                     status: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of attention (vl_decode_attention).
+
+    q [tokens, n_q_heads*head_dim] (or [tokens, n_q_heads, head_dim]; a row
+    stride is allowed, e.g. a view of a packed qkv buffer); k_cache /
+    v_cache [num_slots, n_kv_heads*head_dim] (or 3-D); positions int32
+    [tokens]; seq_start int64 [tokens].  With k / v (new rows, same layout
+    rules) RoPE at the positions (rotary_dim > 0) and the cache append are
+    fused in.  max_seq_len bounds positions + 1 (a sequence's cache capacity):
+    it sizes the split of the positions over CTAs, so pass the real bound.
+    Without `workspace`, a zero-filled per-device workspace is used, which
+    serves calls in stream order on one stream."""
+    _same(q, k_cache, "k_cache")
+    _same(q, v_cache, "v_cache")
+    kvw = n_kv_heads * head_dim
+    num_slots, cs = _rows_of(k_cache, kvw, "k_cache")
+    vslots, vs = _rows_of(v_cache, kvw, "v_cache")
+    if (vslots, vs) != (num_slots, cs):
+        raise VlasrInputError("k_cache and v_cache must have the same shape and row stride")
+    qw = q.shape[-1] * (q.shape[-2] if q.dim() >= 3 else 1)
+    if qw % head_dim:
+        raise VlasrInputError("q rows must be a whole number of heads")
+    nq = qw // head_dim
+    tokens, qs = _rows_of(q, qw, "q")
+    ks = 0
+    if (k is None) != (v is None):
+        raise VlasrInputError("k and v must both be given or both be None")
+    if k is not None:
+        _same(q, k, "k")
+        _same(q, v, "v")
+        kt, ks = _rows_of(k, kvw, "k")
+        vt, vstr = _rows_of(v, kvw, "v")
+        if kt != tokens or vt != tokens or vstr != ks:
+            raise VlasrInputError("k and v must have one row per token and the same row stride")
+    for name, t, dt in (("positions", positions, torch.int32), ("seq_start", seq_start, torch.int64)):
+        _contig(t, name)
+        if t.dtype != dt or t.numel() != tokens:
+            raise VlasrInputError(f"{name} must be {dt} with one entry per token")
+    max_seq_len = int(max_seq_len)
+    if out is None:
+        out = torch.empty((tokens, nq * head_dim), dtype=q.dtype, device=q.device)
+    _same(q, out, "out")
+    ot, os_ = _rows_of(out, nq * head_dim, "out")
+    if ot != tokens:
+        raise VlasrInputError("out must have one row per token")
+    need = decode_attention_workspace_bytes(max(tokens, 1), nq, n_kv_heads, head_dim,
+                                            max(max_seq_len, 1))
+    if workspace is None:
+        workspace = _attn_workspace(q.device, need)
+    check(_lib.load().vl_decode_attention(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(positions),
+        _ptr(seq_start), tokens, nq, n_kv_heads, head_dim, rotary_dim, float(rope_base),
+        float(scale), qs, ks, cs, max_seq_len, num_slots, _ptr(out), os_, _dtype_code(q),
+        _ptr(workspace), workspace.numel() * workspace.element_size(), _ptr(status),
+        _stream(q)), "vl_decode_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Index ops
 # ---------------------------------------------------------------------------
 
