@@ -264,4 +264,7 @@ def load_reference_kernels():
     lib.vlref_weights_bytes.argtypes = [c_void_p]
     lib.vlref_encode_batched.restype = c_int
     lib.vlref_encode_batched.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
+    lib.vlref_decode_batched.restype = c_int
+    lib.vlref_decode_batched.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                         c_void_p, c_void_p, c_void_p, c_void_p]
     return lib

@@ -65,4 +65,42 @@ int vlref_encode_batched(void* weights, const float* mel, int chunks, int fp16_a
   }
 }
 
+// Cross-chunk batched decode (engine.h:95-105, decoder.cu:1372-1800):
+// audio_embeds is the device FP16 projector output [chunks*375, 2048];
+// prompt_ids (host) are shared by every chunk.  out_ids (host) receives
+// [chunks][max_new_tokens] ids, -1 after each chunk's last id (its EOS or
+// the budget); out_lens the count per chunk; the engine's own prefill and
+// decode times are returned in milliseconds.
+int vlref_decode_batched(void* weights, const void* audio_embeds, int chunks,
+                         const int64_t* prompt_ids, int prompt_len, int max_new_tokens,
+                         int fp16_accumulate, int64_t* out_ids, int* out_lens, float* prefill_ms,
+                         float* decode_ms) {
+  try {
+    std::vector<int64_t> prompt(prompt_ids, prompt_ids + (prompt_len > 0 ? prompt_len : 0));
+    DecodeOptions options;
+    options.fp16_accumulate = fp16_accumulate != 0;
+    options.max_new_tokens = max_new_tokens;
+    options.prefill_batched = true;
+    const DecodeBatchResult r =
+        run_decode_batched(static_cast<DeviceWeights*>(weights),
+                           static_cast<const uint16_t*>(audio_embeds), chunks, prompt, options);
+    for (int c = 0; c < chunks; ++c) {
+      const std::vector<int64_t>& ids = r.per_chunk_ids[static_cast<size_t>(c)];
+      int n = 0;
+      for (; n < max_new_tokens && n < static_cast<int>(ids.size()); ++n)
+        out_ids[static_cast<size_t>(c) * max_new_tokens + n] = ids[static_cast<size_t>(n)];
+      out_lens[c] = n;
+      for (int i = n; i < max_new_tokens; ++i)
+        out_ids[static_cast<size_t>(c) * max_new_tokens + i] = -1;
+    }
+    if (prefill_ms) *prefill_ms = r.prefill_ms;
+    if (decode_ms) *decode_ms = r.decode_ms;
+    return 0;
+  } catch (const ModelInputError& e) {
+    return fail(e, 2);
+  } catch (const std::exception& e) {
+    return fail(e, 1);
+  }
+}
+
 }  // extern "C"

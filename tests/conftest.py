@@ -54,3 +54,15 @@ def ref_kernels():
     if lib is None:
         pytest.skip("oracle/_ref/libvlref.so not built (reference sources absent at build time)")
     return lib
+
+
+@pytest.fixture(scope="session")
+def glmasr_ckpt(tmp_path_factory):
+    """A seeded synthetic checkpoint with the full official GLM-ASR-Nano
+    inventory (audio tower, projector, 28-layer text model, 59264-token
+    vocabulary; ~4.5 GB), written once per test session."""
+    from vlasr.checkpoint import AsrModelConfig
+    from vlasr.synth import write_synthetic_checkpoint
+    d = tmp_path_factory.mktemp("glmasr_full")
+    write_synthetic_checkpoint(d, AsrModelConfig(), seed=11)
+    return d

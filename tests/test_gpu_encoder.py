@@ -23,7 +23,7 @@ from helpers import normwise, to_np
 from oracle.encoder_ref import encode_fp32
 from vlasr.checkpoint import load_weights
 from vlasr.encoder import AudioEncoder
-from vlasr.synth import audio_chunks_device, write_synthetic_checkpoint
+from vlasr.synth import audio_chunks_device
 
 pytestmark = pytest.mark.gpu
 
@@ -34,10 +34,8 @@ TOL_ENC = {torch.bfloat16: 4e-2, torch.float16: 8e-3}
 
 
 @pytest.fixture(scope="module")
-def ckpt(tmp_path_factory):
-    d = tmp_path_factory.mktemp("glmasr_synthetic")
-    write_synthetic_checkpoint(d, seed=11)
-    return d
+def ckpt(glmasr_ckpt):
+    return glmasr_ckpt
 
 
 @pytest.fixture(scope="module")

@@ -1,0 +1,259 @@
+"""GLM-ASR text model: batched prefill and lockstep greedy decode over resident
+weights, the decoder-side caller of the fused layer ops.
+
+Computes what the reference's cross-chunk batched decode computes
+(VideoLingo-user native/asr/src/decoder.cu:1372-1800, run_decode_batched):
+
+    prefill, all chunks of the call together (the prompt ids are shared; the
+    audio placeholders take the chunk's projector rows):
+      h = embed(prompt, audio)                           vl_embed_gather
+      28 x { y = RMSNorm1(h)                             vl_add_rmsnorm (fused with the
+                                                         previous layer's residual add)
+             qkv = y Wqkv^T                              one GEMM (q 2048 | k 512 | v 512)
+             RoPE(q, k) at row % L                       vl_rope_inplace (rotary 128)
+             cache[chunk][pos] = k, v                    vl_kv_append
+             a = causal GQA attention (16 q / 4 kv heads) torch SDPA
+             h += a Wo^T; y = RMSNorm2(h)                vl_add_rmsnorm
+             g|u = y Wgu^T; m = silu(g) * u              one GEMM, vl_swiglu
+             delta = m Wd^T }
+      first id = argmax(lm_head(RMSNorm(h + delta)[last row]))
+    lockstep decode, the active chunks only:
+      h = embed(current id)                              vl_embed_gather (row map)
+      28 x { y = RMSNorm1(h); qkv = y Wqkv^T
+             a = attention of the token at its position,  vl_decode_attention (RoPE, KV
+                 GQA over the chunk's cache               append and attention fused)
+             ... as in prefill }
+      next id = argmax(...); a chunk stops after an EOS id (59246, 59253, 59255)
+
+Differences from the reference: every GEMM accumulates in fp32 (its default
+accumulates in fp16), q/k/v and gate/up are single GEMMs, attention keeps
+its scores on chip, the KV cache is not limited to 1024 positions, and the
+per-step host round trip only reads the finished flags.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from ._lib import VlasrInputError
+
+EOS_IDS = (59246, 59253, 59255)
+AUDIO_TOKEN_ID = 59260
+AUDIO_TOKENS_PER_CHUNK = 375
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    layers: int
+    vocab: int
+    rope_base: float = 10000.0
+    eps: float = 1e-5
+
+
+@dataclass
+class DecodeResult:
+    per_chunk_ids: list            # generated ids per chunk, through the first EOS
+    steps: int                     # decode steps executed (lockstep rounds incl. the first id)
+    forced_agreement: list | None = None   # teacher forcing: (argmax, margin) per step and chunk
+
+
+class TextDecoder:
+    """Resident text-model weights in one compute dtype and the prefill /
+    decode launch sequences.  `weights` maps the official names
+    (language_model.*) to device tensors."""
+
+    def __init__(self, weights: dict, *, heads: int = 16, kv_heads: int = 4,
+                 dtype=torch.bfloat16, max_seq_len: int = 1024,
+                 audio_token_id: int = AUDIO_TOKEN_ID, eos_ids=EOS_IDS):
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise VlasrInputError("TextDecoder computes in bf16 or fp16")
+        emb = weights["language_model.model.embed_tokens.weight"]
+        if emb.device.type != "cuda":
+            raise VlasrInputError("TextDecoder weights must be CUDA tensors")
+        vocab, hidden = emb.shape
+        layers = 0
+        while f"language_model.model.layers.{layers}.mlp.down_proj.weight" in weights:
+            layers += 1
+        ffn = weights["language_model.model.layers.0.mlp.gate_proj.weight"].shape[0]
+        self.shape = DecoderShape(hidden=hidden, heads=heads, kv_heads=kv_heads,
+                                  head_dim=hidden // heads, ffn=ffn, layers=layers, vocab=vocab)
+        self.dtype = dtype
+        self.device = emb.device
+        self.max_seq_len = int(max_seq_len)
+        self.audio_token_id = int(audio_token_id)
+        self.eos_ids = tuple(int(e) for e in eos_ids)
+
+        def w(name):
+            return weights[name].to(device=self.device, dtype=dtype).contiguous()
+
+        self.embed = w("language_model.model.embed_tokens.weight")
+        self.lm_head_t = w("language_model.lm_head.weight").t()
+        self.norm_w = w("language_model.model.norm.weight")
+        self.layer_w = []
+        for l in range(layers):
+            p = f"language_model.model.layers.{l}."
+            self.layer_w.append({
+                "ln1": w(p + "input_layernorm.weight"),
+                "qkv_t": torch.cat([w(p + f"self_attn.{n}_proj.weight") for n in "qkv"], 0).t(),
+                "o_t": w(p + "self_attn.o_proj.weight").t(),
+                "ln2": w(p + "post_attention_layernorm.weight"),
+                "gu_t": torch.cat([w(p + "mlp.gate_proj.weight"),
+                                   w(p + "mlp.up_proj.weight")], 0).t(),
+                "down_t": w(p + "mlp.down_proj.weight").t(),
+            })
+        self.eos = torch.tensor(self.eos_ids, device=self.device, dtype=torch.int64)
+
+    # ------------------------------------------------------------------
+    def _mlp(self, lw: dict, h: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
+        """h += o; y = RMSNorm2(h); return down(silu(gate(y)) * up(y))."""
+        s = self.shape
+        y = ops.add_rmsnorm(h, o, lw["ln2"], eps=s.eps)
+        gu = y @ lw["gu_t"]
+        m = ops.swiglu(gu[:, :s.ffn], gu[:, s.ffn:])
+        return m @ lw["down_t"]
+
+    def _argmax(self, h: torch.Tensor, delta: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        s = self.shape
+        y = ops.add_rmsnorm(h, delta, self.norm_w, eps=s.eps)
+        logits = (y @ self.lm_head_t).float()
+        return logits.argmax(-1), logits
+
+    def prefill(self, audio: torch.Tensor, prompt: torch.Tensor, k_cache, v_cache,
+                chunk_slots: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Run the prompt of every chunk; fill the caches; -> (first ids, logits)."""
+        s = self.shape
+        chunks, L = audio.shape[0], prompt.numel()
+        h = ops.embed_gather(prompt, self.embed, audio=audio, audio_token_id=self.audio_token_id,
+                             shared_ids=True, batch=chunks).view(chunks * L, s.hidden)
+        qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        pos_slots = (chunk_slots.view(chunks, 1)
+                     + torch.arange(L, device=self.device).view(1, L)).reshape(-1)
+        delta = None
+        for l, lw in enumerate(self.layer_w):
+            y = ops.add_rmsnorm(h, delta, lw["ln1"], eps=s.eps)
+            qkv = y @ lw["qkv_t"]
+            q, k, v = qkv[:, :qw], qkv[:, qw:qw + kw], qkv[:, qw + kw:]
+            ops.rope_(q, k, head_dim=s.head_dim, rotary_dim=s.head_dim, base=s.rope_base,
+                      seq_len=L)
+            ops.kv_append(k, v, k_cache[l], v_cache[l], pos_slots)
+            qh = q.view(chunks, L, s.heads, s.head_dim).transpose(1, 2)
+            kh = k.view(chunks, L, s.kv_heads, s.head_dim).transpose(1, 2)
+            vh = v.view(chunks, L, s.kv_heads, s.head_dim).transpose(1, 2)
+            a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
+            a = a.transpose(1, 2).reshape(chunks * L, qw)
+            delta = self._mlp(lw, h, a @ lw["o_t"])
+        last = torch.arange(chunks, device=self.device) * L + (L - 1)
+        return self._argmax(h[last].contiguous(), delta[last].contiguous())
+
+    def step(self, ids: torch.Tensor, active: torch.Tensor, positions: torch.Tensor,
+             k_cache, v_cache, chunk_slots: torch.Tensor, workspace: torch.Tensor):
+        """One lockstep decode step for the active chunks: ids [chunks] (int64)
+        are the current tokens, positions [chunks] (int32) their positions."""
+        s = self.shape
+        qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        h = ops.embed_gather(ids.view(-1, 1), self.embed, row_map=active).view(-1, s.hidden)
+        pos = positions[active.long()].contiguous()
+        start = chunk_slots[active.long()].contiguous()
+        delta = None
+        for l, lw in enumerate(self.layer_w):
+            y = ops.add_rmsnorm(h, delta, lw["ln1"], eps=s.eps)
+            qkv = y @ lw["qkv_t"]
+            a = ops.decode_attention(qkv[:, :qw], k_cache[l], v_cache[l], pos, start,
+                                     n_kv_heads=s.kv_heads, head_dim=s.head_dim,
+                                     max_seq_len=self.max_seq_len, k=qkv[:, qw:qw + kw],
+                                     v=qkv[:, qw + kw:], rotary_dim=s.head_dim,
+                                     rope_base=s.rope_base, workspace=workspace)
+            delta = self._mlp(lw, h, a @ lw["o_t"])
+        return self._argmax(h, delta)
+
+    def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,
+                 forced_ids: list | None = None) -> DecodeResult:
+        """audio [chunks*375, hidden] (or [chunks, 375, hidden]) projector rows;
+        prompt_ids: the shared prompt (int64).  Greedy decode of up to
+        max_new_tokens ids per chunk (the first from the prefill).
+
+        forced_ids (tests): per-chunk id lists fed back instead of the argmax
+        (teacher forcing); the result then records this decoder's argmax and
+        its top-1/top-2 logit margin at every step."""
+        s = self.shape
+        prompt = torch.as_tensor(prompt_ids, dtype=torch.int64).to(self.device).contiguous()
+        L = prompt.numel()
+        if audio.dim() == 2:
+            audio = audio.view(-1, AUDIO_TOKENS_PER_CHUNK, s.hidden)
+        audio = audio.to(self.dtype).contiguous()
+        chunks = audio.shape[0]
+        if L + max_new_tokens > self.max_seq_len:
+            raise VlasrInputError("prompt plus budget exceeds the decoder's max_seq_len")
+        if chunks < 1:
+            raise VlasrInputError("at least one chunk is required")
+        kw = s.kv_heads * s.head_dim
+        slots = chunks * self.max_seq_len
+        k_cache = [torch.empty(slots, kw, dtype=self.dtype, device=self.device)
+                   for _ in range(s.layers)]
+        v_cache = [torch.empty(slots, kw, dtype=self.dtype, device=self.device)
+                   for _ in range(s.layers)]
+        chunk_slots = torch.arange(chunks, device=self.device, dtype=torch.int64) * self.max_seq_len
+        ws = torch.zeros(ops.decode_attention_workspace_bytes(chunks, s.heads, s.kv_heads,
+                                                              s.head_dim, self.max_seq_len),
+                         dtype=torch.uint8, device=self.device)
+
+        first, logits = self.prefill(audio, prompt, k_cache, v_cache, chunk_slots)
+        out = torch.full((max_new_tokens, chunks), -1, dtype=torch.int64, device=self.device)
+        agreement = [] if forced_ids is not None else None
+
+        def record(step_ids, lg, rows):
+            if agreement is None:
+                return
+            top2 = lg.topk(2, dim=-1)
+            margin = (top2.values[:, 0] - top2.values[:, 1]).tolist()
+            agreement.append({int(c): (int(i), float(m))
+                              for c, i, m in zip(rows.tolist(), step_ids.tolist(), margin)})
+
+        all_rows = torch.arange(chunks, device=self.device, dtype=torch.int32)
+        record(first, logits, all_rows)
+        current = first.clone()
+        if forced_ids is not None:
+            current = torch.tensor([f[0] for f in forced_ids], device=self.device)
+        out[0] = current
+        finished = torch.isin(current, self.eos)
+        positions = torch.full((chunks,), L, dtype=torch.int32, device=self.device)
+        steps = 1
+        for step in range(1, max_new_tokens):
+            fin = finished.tolist()
+            if forced_ids is not None:
+                fin = [len(forced_ids[c]) <= step for c in range(chunks)]
+            act = [c for c in range(chunks) if not fin[c]]
+            if not act:
+                break
+            active = torch.tensor(act, device=self.device, dtype=torch.int32)
+            nxt, lg = self.step(current, active, positions, k_cache, v_cache, chunk_slots, ws)
+            record(nxt, lg, active)
+            rows = active.long()
+            if forced_ids is not None:
+                nxt = torch.tensor([forced_ids[c][step] for c in act], device=self.device)
+            current[rows] = nxt
+            out[step, rows] = nxt
+            finished[rows] = torch.isin(nxt, self.eos)
+            positions[rows] += 1
+            steps += 1
+        ids = out.t().tolist()
+        per_chunk = []
+        for c in range(chunks):
+            seq = []
+            for i in ids[c]:
+                if i < 0:
+                    break
+                seq.append(i)
+                if i in self.eos_ids:
+                    break
+            per_chunk.append(seq)
+        return DecodeResult(per_chunk_ids=per_chunk, steps=steps, forced_agreement=agreement)
