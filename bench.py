@@ -71,6 +71,12 @@ def parse() -> argparse.Namespace:
                    help="SDPA backend of the encoder's attention")
     p.add_argument("--gemm-acc", type=int, choices=[16, 32], default=16,
                    help="reference encoder arm: GEMM accumulation (its default is 16)")
+    p.add_argument("--asr", action="store_true",
+                   help="engine mode: host PCM -> log-mel -> audio tower -> text decoder -> ids "
+                        "(vlasr.engine) on a seeded synthetic checkpoint; with --impl reference, "
+                        "the reference engine's mel + run_encode_batched + run_decode_batched")
+    p.add_argument("--asr-chunks", type=int, default=16, help="30 s chunks per engine call")
+    p.add_argument("--asr-tokens", type=int, default=64, help="token budget per chunk")
     p.add_argument("--op", default=None,
                    help="profiling mode: run only this op of the per-op table "
                         "(warmup + steps launches, no flush) and print its timing")
@@ -567,6 +573,156 @@ def run_encoder_bench(args) -> None:
 
 
 # ---------------------------------------------------------------------------
+# engine mode (mel + encoder + decoder, the reference's `transcribe`)
+# ---------------------------------------------------------------------------
+
+ASR_METRIC = "engine audio-seconds/s (log-mel + audio tower + projector + greedy decode per 30 s chunk)"
+ASR_PROMPT = [151, 2222, 3333] + [59260] * 375 + [4444, 5555, 6666, 77]
+
+
+def run_asr_bench(args) -> None:
+    """One GPU: the whole engine call on `--asr-chunks` chunks of host PCM with
+    a `--asr-tokens` budget, as the reference CLI's transcribe runs it
+    (native/asr/src/main_m0.cu:448-470: mel, encoder in groups of 8, batched
+    decode).  Both arms read the same seeded synthetic checkpoint (the full
+    official inventory; random weights, so EOS is rare and every chunk
+    usually decodes the whole budget) and the same PCM and prompt."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import shutil
+    import tempfile
+
+    import numpy as np
+    import torch
+    import vlasr
+    from vlasr.checkpoint import AsrModelConfig
+    from vlasr.synth import audio_chunks, write_synthetic_checkpoint
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    vlasr.load()
+    chunks, budget = args.asr_chunks, args.asr_tokens
+    pcm = audio_chunks(chunks, seed=5)
+    ckpt = tempfile.mkdtemp(prefix="vl_glmasr_")
+    base = {"metric": ASR_METRIC, "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "data": "synthetic (seeded audio; seeded synthetic checkpoint "
+            "with the official GLM-ASR inventory)"}
+    try:
+        write_synthetic_checkpoint(ckpt, AsrModelConfig(), seed=11)
+        sampler = ClockSampler(0)
+        if args.impl == "reference":
+            import ctypes
+            import oracle
+            lib = oracle.load_reference_kernels()
+            if lib is None:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "oracle/_ref/libvlref.so not built"}), flush=True)
+                return
+            handle = lib.vlref_load_weights(ckpt.encode(), 64 << 30)
+            if not handle:
+                raise SystemExit(lib.vlref_last_error().decode())
+            prompt = np.asarray(ASR_PROMPT, np.int64)
+            audio = torch.empty(chunks * 375, 2048, dtype=torch.float16, device=dev)
+            out_ids = np.zeros((chunks, budget), np.int64)
+            lens = np.zeros(chunks, np.int32)
+            mel = np.empty((chunks, 128, 3000), np.float32)
+            split = {"mel_ms": 0.0, "encode_ms": 0.0, "decode_ms": 0.0}
+
+            def call():
+                t0 = time.perf_counter()
+                rc = lib.vlref_compute_mel_batched(pcm.ctypes.data_as(ctypes.c_void_p), chunks,
+                                                   mel.ctypes.data_as(ctypes.c_void_p))
+                t1 = time.perf_counter()
+                for g0 in range(0, chunks, 8):
+                    g = min(8, chunks - g0)
+                    rc = rc or lib.vlref_encode_batched(
+                        handle, mel[g0:g0 + g].ctypes.data_as(ctypes.c_void_p), g, 1,
+                        ctypes.c_void_p(audio.data_ptr() + g0 * 375 * 2048 * 2))
+                torch.cuda.synchronize()
+                t2 = time.perf_counter()
+                rc = rc or lib.vlref_decode_batched(
+                    handle, ctypes.c_void_p(audio.data_ptr()), chunks,
+                    prompt.ctypes.data_as(ctypes.c_void_p), len(ASR_PROMPT), budget, 1,
+                    out_ids.ctypes.data_as(ctypes.c_void_p), lens.ctypes.data_as(ctypes.c_void_p),
+                    None, None)
+                t3 = time.perf_counter()
+                if rc:
+                    raise SystemExit(lib.vlref_last_error().decode())
+                split["mel_ms"] += (t1 - t0) * 1e3
+                split["encode_ms"] += (t2 - t1) * 1e3
+                split["decode_ms"] += (t3 - t2) * 1e3
+
+            for _ in range(args.warmup):
+                call()
+            split = dict.fromkeys(split, 0.0)
+            sampler.start()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                call()
+            ms = (time.perf_counter() - t0) * 1e3 / args.steps
+            clocks = sampler.stop()
+            lib.vlref_free_weights(handle)
+            tokens = int(lens.sum())
+            value = chunks * AUDIO_SECONDS_PER_CHUNK / (ms / 1e3)
+            line = {"impl": "reference", **base, "value": round(value, 1),
+                    "ms_per_step": round(ms, 2), "dtype": "fp16",
+                    "config": {"workload": "engine", "chunks_per_step": chunks,
+                               "token_budget": budget, "prompt_tokens": len(ASR_PROMPT),
+                               "tokens_generated": tokens, "gemm_acc": "fp16 (its default)",
+                               "api": "compute_mel_batched + run_encode_batched (groups of 8) + "
+                                      "run_decode_batched, as main_m0.cu transcribe"},
+                    "stages_ms": {k: round(v / args.steps, 2) for k, v in split.items()},
+                    "e2e": {"value": round(value, 1), "unit": "audio-s/s",
+                            "h2d_bytes_per_step": int(pcm.nbytes),
+                            "d2h_bytes_per_step": int(out_ids.nbytes)},
+                    "clocks": clocks}
+            print(json.dumps(line), flush=True)
+            return
+
+        from vlasr.engine import AsrEngine
+        eng = AsrEngine(ckpt, device=dev)
+        pcm_host = torch.from_numpy(pcm).pin_memory()
+        result = {}
+
+        def call():
+            result["ids"] = eng.transcribe_ids(pcm_host, ASR_PROMPT, max_new_tokens=budget)
+
+        for _ in range(args.warmup):
+            call()
+        split = {"mel_ms": 0.0, "encode_ms": 0.0, "decode_ms": 0.0, "prefill_ms": 0.0,
+                 "decode_steps_ms": 0.0}
+        sampler.start()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            call()
+            t = eng.timings
+            split["mel_ms"] += t.mel_ms
+            split["encode_ms"] += t.encode_ms
+            split["decode_ms"] += t.decode_ms
+            split["prefill_ms"] += t.prefill_ms
+            split["decode_steps_ms"] += t.steps_ms
+        ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        clocks = sampler.stop()
+        tokens = sum(len(x) for x in result["ids"])
+        value = chunks * AUDIO_SECONDS_PER_CHUNK / (ms / 1e3)
+        line = {**base, "value": round(value, 1), "ms_per_step": round(ms, 2), "dtype": "bf16",
+                "config": {"workload": "engine", "chunks_per_step": chunks,
+                           "token_budget": budget, "prompt_tokens": len(ASR_PROMPT),
+                           "tokens_generated": tokens, "gemm_acc": "fp32",
+                           "api": "vlasr.engine.AsrEngine.transcribe_ids (pinned host PCM in, "
+                                  "ids out)"},
+                "stages_ms": {k: round(v / args.steps, 2) for k, v in split.items()},
+                "e2e": {"value": round(value, 1), "unit": "audio-s/s",
+                        "h2d_bytes_per_step": int(pcm.nbytes),
+                        "d2h_bytes_per_step": tokens * 8},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    finally:
+        shutil.rmtree(ckpt, ignore_errors=True)
+
+
+# ---------------------------------------------------------------------------
 # main arm
 # ---------------------------------------------------------------------------
 
@@ -574,6 +730,9 @@ def main() -> None:
     args = parse()
     if args.encoder:
         run_encoder_bench(args)
+        return
+    if args.asr:
+        run_asr_bench(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)

@@ -131,3 +131,11 @@ def test_decoder_rejects(decoders, audio16):
     dec = decoders[torch.float16]
     with pytest.raises(vlasr.VlasrInputError, match="max_seq_len"):
         dec.generate(audio16, PROMPT, max_new_tokens=1000)
+
+
+def test_graph_replay_matches_eager_steps(decoders, audio16):
+    dec = decoders[torch.bfloat16]
+    eager = dec.generate(audio16, PROMPT, max_new_tokens=12, graphs=False).per_chunk_ids
+    graphed = dec.generate(audio16, PROMPT, max_new_tokens=12, graphs=True).per_chunk_ids
+    torch.cuda.synchronize()
+    assert graphed == eager

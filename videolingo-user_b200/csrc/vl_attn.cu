@@ -39,6 +39,7 @@
 // q and the probabilities enter the tensor cores in the storage type (the
 // reference also rounds the rotated q to it); scores, softmax and the
 // output accumulate in fp32.
+#include <atomic>
 #include <cmath>
 
 #include "vl_common.cuh"
@@ -524,9 +525,18 @@ cudaError_t launch_typed(const DecodeAttnArgs& a, cudaStream_t stream) {
   static_assert(smem <= 227 * 1024, "decode attention shared memory");
   auto kernel = decode_attention_kernel<T, HD, G>;
   if (smem > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    // once per device and instantiation, so that later launches (and CUDA
+    // graph captures) make no further runtime calls
+    static std::atomic<bool> configured[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
+    }
   }
   // tokens on x (up to 2^31 - 1), kv heads on y, splits (<= 64) on z
   const dim3 grid(static_cast<unsigned>(a.tokens), static_cast<unsigned>(a.n_kv_heads),

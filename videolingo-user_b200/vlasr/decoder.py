@@ -28,7 +28,9 @@ Computes what the reference's cross-chunk batched decode computes
 Differences from the reference: every GEMM accumulates in fp32 (its default
 accumulates in fp16), q/k/v and gate/up are single GEMMs, attention keeps
 its scores on chip, the KV cache is not limited to 1024 positions, and the
-per-step host round trip only reads the finished flags.
+decode step (about 230 launches) is captured once in a CUDA graph and
+replayed, with the finished flags read every 8 steps instead of a host round
+trip and a re-compaction per step.
 """
 
 from __future__ import annotations
@@ -111,6 +113,8 @@ class TextDecoder:
                 "down_t": w(p + "mlp.down_proj.weight").t(),
             })
         self.eos = torch.tensor(self.eos_ids, device=self.device, dtype=torch.int64)
+        self._states: dict = {}
+        self.last_timings = (0.0, 0.0)   # (prefill ms, decode-steps ms) of the last graphed call
 
     # ------------------------------------------------------------------
     def _mlp(self, lw: dict, h: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
@@ -175,8 +179,90 @@ class TextDecoder:
             delta = self._mlp(lw, h, a @ lw["o_t"])
         return self._argmax(h, delta)
 
+    def _state(self, chunks: int) -> dict:
+        """Per chunk count: KV caches, decode workspace and the step buffers a
+        captured graph points at (kept for the next call of the same size)."""
+        st = self._states.get(chunks)
+        if st is not None:
+            return st
+        self._states.clear()        # one size at a time: free the previous caches first
+        s, dev = self.shape, self.device
+        kw = s.kv_heads * s.head_dim
+        slots = chunks * self.max_seq_len
+        st = {
+            "k_cache": [torch.empty(slots, kw, dtype=self.dtype, device=dev)
+                        for _ in range(s.layers)],
+            "v_cache": [torch.empty(slots, kw, dtype=self.dtype, device=dev)
+                        for _ in range(s.layers)],
+            "chunk_slots": torch.arange(chunks, device=dev, dtype=torch.int64) * self.max_seq_len,
+            "ws": torch.zeros(ops.decode_attention_workspace_bytes(
+                chunks, s.heads, s.kv_heads, s.head_dim, self.max_seq_len),
+                dtype=torch.uint8, device=dev),
+            "out": torch.full((self.max_seq_len, chunks), -1, dtype=torch.int64, device=dev),
+            "cur": torch.zeros(chunks, dtype=torch.int64, device=dev),
+            "fin": torch.zeros(chunks, dtype=torch.bool, device=dev),
+            "pos": torch.zeros(chunks, dtype=torch.int32, device=dev),
+            "step": torch.ones((), dtype=torch.int64, device=dev),
+            "rows": torch.arange(chunks, device=dev, dtype=torch.int32),
+            "lanes": torch.arange(chunks, device=dev, dtype=torch.int64),
+            "frozen": torch.full((chunks,), self.eos_ids[1], dtype=torch.int64, device=dev),
+            "graph": None,
+        }
+        self._states[chunks] = st
+        return st
+
+    def _decode_body(self, st: dict) -> None:
+        """One lockstep step over every chunk of `st` (device state only)."""
+        chunks = st["cur"].numel()
+        nxt, _ = self.step(st["cur"], st["rows"], st["pos"], st["k_cache"], st["v_cache"],
+                           st["chunk_slots"], st["ws"])
+        nxt = torch.where(st["fin"], st["frozen"], nxt)
+        st["out"].view(-1).index_copy_(0, st["step"] * chunks + st["lanes"], nxt)
+        st["fin"].logical_or_(torch.isin(nxt, self.eos))
+        st["cur"].copy_(nxt)
+        st["pos"].add_(1)
+        st["step"].add_(1)
+
+    def _generate_graphed(self, st: dict, first: torch.Tensor, L: int,
+                          max_new_tokens: int) -> torch.Tensor:
+        """Lockstep decode with the step captured in a CUDA graph (once per
+        chunk count; later calls replay it).
+
+        Every chunk stays in the batch; a finished chunk emits 59253 (the
+        reference's argmax_mapped_kernel freeze) and its rows are ignored when
+        the ids are collected.  Without a graph yet, step 1 runs eagerly (it
+        also warms the libraries up) before the capture; the finished flags
+        are read every 8 steps."""
+        out = st["out"]
+        out.fill_(-1)
+        out[0] = first
+        st["cur"].copy_(first)
+        torch.isin(first, self.eos, out=st["fin"])
+        st["pos"].fill_(L)
+        st["step"].fill_(1)
+        if max_new_tokens <= 1:
+            return out[:max_new_tokens]
+        dev = self.device
+        step = 1
+        if st["graph"] is None:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                self._decode_body(st)                   # step 1, eagerly
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    self._decode_body(st)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            st["graph"] = graph
+            step = 2
+        for step in range(step, max_new_tokens):
+            if step % 8 == 0 and bool(st["fin"].all()):
+                break
+            st["graph"].replay()
+        return out[:max_new_tokens]
+
     def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,
-                 forced_ids: list | None = None) -> DecodeResult:
+                 forced_ids: list | None = None, graphs: bool = True) -> DecodeResult:
         """audio [chunks*375, hidden] (or [chunks, 375, hidden]) projector rows;
         prompt_ids: the shared prompt (int64).  Greedy decode of up to
         max_new_tokens ids per chunk (the first from the prefill).
@@ -195,18 +281,20 @@ class TextDecoder:
             raise VlasrInputError("prompt plus budget exceeds the decoder's max_seq_len")
         if chunks < 1:
             raise VlasrInputError("at least one chunk is required")
-        kw = s.kv_heads * s.head_dim
-        slots = chunks * self.max_seq_len
-        k_cache = [torch.empty(slots, kw, dtype=self.dtype, device=self.device)
-                   for _ in range(s.layers)]
-        v_cache = [torch.empty(slots, kw, dtype=self.dtype, device=self.device)
-                   for _ in range(s.layers)]
-        chunk_slots = torch.arange(chunks, device=self.device, dtype=torch.int64) * self.max_seq_len
-        ws = torch.zeros(ops.decode_attention_workspace_bytes(chunks, s.heads, s.kv_heads,
-                                                              s.head_dim, self.max_seq_len),
-                         dtype=torch.uint8, device=self.device)
-
+        st = self._state(chunks)
+        k_cache, v_cache = st["k_cache"], st["v_cache"]
+        chunk_slots, ws = st["chunk_slots"], st["ws"]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
         first, logits = self.prefill(audio, prompt, k_cache, v_cache, chunk_slots)
+        ev[1].record()
+        if graphs and forced_ids is None:
+            out = self._generate_graphed(st, first, L, max_new_tokens)
+            ev[2].record()
+            result = DecodeResult(per_chunk_ids=self._collect(out, chunks),
+                                  steps=int((out >= 0).any(1).sum()))
+            self.last_timings = (ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]))
+            return result
         out = torch.full((max_new_tokens, chunks), -1, dtype=torch.int64, device=self.device)
         agreement = [] if forced_ids is not None else None
 
@@ -245,6 +333,11 @@ class TextDecoder:
             finished[rows] = torch.isin(nxt, self.eos)
             positions[rows] += 1
             steps += 1
+        return DecodeResult(per_chunk_ids=self._collect(out, chunks), steps=steps,
+                            forced_agreement=agreement)
+
+    def _collect(self, out: torch.Tensor, chunks: int) -> list[list[int]]:
+        """out [steps, chunks] -> per chunk, the ids through the first EOS."""
         ids = out.t().tolist()
         per_chunk = []
         for c in range(chunks):
@@ -256,4 +349,4 @@ class TextDecoder:
                 if i in self.eos_ids:
                     break
             per_chunk.append(seq)
-        return DecodeResult(per_chunk_ids=per_chunk, steps=steps, forced_agreement=agreement)
+        return per_chunk

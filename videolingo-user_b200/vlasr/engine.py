@@ -31,7 +31,9 @@ MAX_CHUNKS = 128   # the reference engine's limit per call (native.py:155-157)
 class EngineTimings:
     mel_ms: float = 0.0
     encode_ms: float = 0.0
-    decode_ms: float = 0.0
+    decode_ms: float = 0.0       # prefill + decode steps
+    prefill_ms: float = 0.0
+    steps_ms: float = 0.0
 
 
 def pad_to_chunks(pcm: np.ndarray, chunk_samples: int = CHUNK_SAMPLES) -> np.ndarray:
@@ -91,5 +93,5 @@ class AsrEngine:
         ev[3].record()
         torch.cuda.synchronize(self.device)
         self.timings = EngineTimings(ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
-                                     ev[2].elapsed_time(ev[3]))
+                                     ev[2].elapsed_time(ev[3]), *self.decoder.last_timings)
         return result.per_chunk_ids
