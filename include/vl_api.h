@@ -342,6 +342,41 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
                                   int64_t out_row_stride, int dtype, void* workspace,
                                   size_t workspace_bytes, int32_t* status, void* stream);
 
+/*
+ * Decode-step linear layer: y = x W^T for rows <= 64 token rows (W [n][k]
+ * row-major, as nn.Linear and the checkpoint store it), fp32 accumulation,
+ * one rounding to the storage type, with the neighbouring memory-bound steps
+ * of the reference's decode layer fused in (native/asr/src/decoder.cu:
+ * rmsnorm_kernel :81-101, the `gemm` projections :1002-1033,
+ * residual_add_kernel :933-938, silu_mul_kernel :103-109):
+ *
+ * prologue  norm_weight NULL: A = x.
+ *           norm_weight given: A = round(x * rsqrtf(S/k + eps) * w_norm[k])
+ *           with S = sum over p < ssq_in_parts of ssq_in[p*rows + row] (the
+ *           partial sums written by a RESIDUAL call, summed in order).
+ * epilogue  VL_LINEAR_STORE    y[row][j] = round(acc), j < n
+ *           VL_LINEAR_SWIGLU   W = [gate rows n/2; up rows n/2];
+ *                              y[row][j] = round(silu(round(acc_gate)) *
+ *                              round(acc_up)), j < n/2
+ *           VL_LINEAR_RESIDUAL y is the residual stream, updated in place:
+ *                              y[row][j] = round(y + round(acc)); if
+ *                              ssq_out, ssq_out[(j/16)*rows + row] = sum of
+ *                              the squares of the 16 new values j..j+15.
+ * Requires k % 256 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y 16-byte
+ * aligned with row strides that are multiples of 8 elements, x not
+ * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
+ */
+#define VL_LINEAR_STORE 0
+#define VL_LINEAR_SWIGLU 1
+#define VL_LINEAR_RESIDUAL 2
+#define VL_LINEAR_MAX_ROWS 64
+
+VL_EXPORT int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weight,
+                               const float* ssq_in, int ssq_in_parts, float eps,
+                               const void* w, int64_t n, int64_t k, void* y,
+                               int64_t y_row_stride, float* ssq_out, int64_t rows,
+                               int epilogue, int dtype, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

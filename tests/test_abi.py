@@ -31,6 +31,7 @@ def test_header_declares_the_expected_ops():
     for name in ("vl_logmel", "vl_add_layernorm", "vl_add_rmsnorm", "vl_gelu_erf", "vl_swiglu",
                  "vl_rope_inplace", "vl_embed_gather", "vl_kv_append", "vl_rope_kv_append",
                  "vl_decode_attention", "vl_decode_attention_workspace_bytes",
+                 "vl_decode_linear",
                  "vl_last_error", "vl_logmel_workspace_bytes"):
         assert name in syms
 
@@ -166,6 +167,26 @@ def test_decode_attention_rejects(lib):
     assert lib.vl_decode_attention_workspace_bytes(64, 16, 4, 128, 4096) >= 64 * 4 * 4
     assert lib.vl_decode_attention_workspace_bytes(0, 16, 4, 128, 4096) == 0
     assert lib.vl_decode_attention_workspace_bytes(1, 16, 3, 128, 4096) == 0
+
+
+def test_decode_linear_rejects(lib):
+    def call(x=FAKE, xs=2048, g=None, ssq=None, parts=0, eps=1e-5, w=FAKE * 2, n=3072, k=2048,
+             y=FAKE * 1000, ys=3072, so=None, rows=16, epi=0, dtype=2):
+        return lib.vl_decode_linear(x, xs, g, ssq, parts, eps, w, n, k, y, ys, so, rows, epi,
+                                    dtype, None)
+
+    assert call(x=None) == 2 and "null" in _err(lib)
+    assert call(dtype=0) == 2 and "dtype" in _err(lib)
+    assert call(epi=7) == 2 and "epilogue" in _err(lib)
+    assert call(rows=65) == 2 and "rows" in _err(lib)
+    assert call(k=2000, xs=2000) == 2 and "multiple of 256" in _err(lib)
+    assert call(n=3000) == 2 and "multiple of 16" in _err(lib)
+    assert call(n=3056, epi=1, ys=1528) == 2 and "multiple of 32" in _err(lib)
+    assert call(xs=2052) == 2 and "strides" in _err(lib)
+    assert call(x=FAKE + 2) == 2 and "aligned" in _err(lib)
+    assert call(g=FAKE * 3) == 2 and "ssq_in" in _err(lib)
+    assert call(so=FAKE * 4) == 2 and "RESIDUAL" in _err(lib)
+    assert call(y=FAKE) == 2 and "overlaps" in _err(lib)
 
 
 def test_error_is_thread_local(lib):

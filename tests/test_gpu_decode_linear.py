@@ -1,0 +1,130 @@
+"""GPU: the decode-step linear layer (vl_decode_linear) against a torch fp32
+reference of the same math with the reference's rounding points
+(native/asr/src/decoder.cu: `gemm` outputs rounded to the storage type,
+rmsnorm_kernel, residual_add_kernel, silu_mul_kernel), for every epilogue,
+with and without the RMSNorm prologue, at 1..64 token rows."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import vlasr
+from helpers import TOL, normwise, to_np
+
+pytestmark = pytest.mark.gpu
+
+DT = [(torch.bfloat16, "bf16"), (torch.float16, "f16")]
+
+
+def _rand(shape, dev, dtype, seed, std=1.0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std).to(dtype).to(dev)
+
+
+def _r(t, dtype):
+    return t.to(dtype).float()
+
+
+def _norm_ref(h, gamma, ssq_rows, k, dtype, eps=1e-5):
+    inv = torch.rsqrt(ssq_rows / k + eps)
+    return _r(h.float() * inv[:, None] * gamma.float(), dtype)
+
+
+@pytest.mark.parametrize("dtype,name", DT, ids=["bf16", "f16"])
+@pytest.mark.parametrize("rows", [1, 7, 16, 33, 64])
+def test_store(dev, dtype, name, rows):
+    x = _rand((rows, 2048), dev, dtype, rows)
+    w = _rand((3072, 2048), dev, dtype, 100 + rows, 2048 ** -0.5)
+    y = vlasr.decode_linear(x, w)
+    ref = _r(x.float() @ w.float().t(), dtype)
+    torch.cuda.synchronize()
+    assert normwise(to_np(y), to_np(ref)) <= TOL[name]
+
+
+@pytest.mark.parametrize("dtype,name", DT, ids=["bf16", "f16"])
+def test_swiglu(dev, dtype, name):
+    rows, k, ffn = 16, 2048, 6144
+    x = _rand((rows, k), dev, dtype, 1)
+    w = _rand((2 * ffn, k), dev, dtype, 2, k ** -0.5 * 2)
+    y = vlasr.decode_linear(x, w, epilogue="swiglu")
+    gu = x.float() @ w.float().t()
+    g, u = _r(gu[:, :ffn], dtype), _r(gu[:, ffn:], dtype)
+    ref = _r(g / (1 + torch.exp(-g)) * u, dtype)
+    torch.cuda.synchronize()
+    assert y.shape == (rows, ffn)
+    assert normwise(to_np(y), to_np(ref)) <= TOL[name]
+
+
+@pytest.mark.parametrize("dtype,name", DT, ids=["bf16", "f16"])
+def test_residual_and_norm_chain(dev, dtype, name):
+    """down-projection with the residual epilogue, then a projection whose
+    RMSNorm prologue uses the partial sums it produced (a decode layer's
+    ffn -> next layer's q|k|v)."""
+    rows, hid, ffn = 12, 2048, 6144
+    h = _rand((rows, hid), dev, dtype, 3)
+    m = _rand((rows, ffn), dev, dtype, 4)
+    wd = _rand((hid, ffn), dev, dtype, 5, ffn ** -0.5)
+    gamma = _rand(hid, dev, dtype, 6, 0.02) + 1
+    wq = _rand((3072, hid), dev, dtype, 7, hid ** -0.5)
+    h_ref = _r(h.float() + _r(m.float() @ wd.float().t(), dtype), dtype)
+    ssq = torch.empty(hid // 16, rows, dtype=torch.float32, device=dev)
+    vlasr.decode_linear(m, wd, epilogue="residual", out=h, ssq_out=ssq)
+    torch.cuda.synchronize()
+    assert normwise(to_np(h), to_np(h_ref)) <= TOL[name]
+    # partial sums are exact sums of squares of the new residual values
+    hs = h.float().view(rows, hid // 16, 16)
+    assert torch.allclose(ssq, (hs * hs).sum(-1).t(), rtol=1e-5, atol=1e-5)
+    q = vlasr.decode_linear(h, wq, norm_weight=gamma, ssq_in=ssq)
+    xn = _norm_ref(h, gamma, (h.float() ** 2).sum(-1), hid, dtype)
+    ref = _r(xn @ wq.float().t(), dtype)
+    torch.cuda.synchronize()
+    assert normwise(to_np(q), to_np(ref)) <= TOL[name]
+
+
+def test_norm_prologue_matches_add_rmsnorm(dev):
+    """RMSNorm prologue == vl_add_rmsnorm then the plain projection."""
+    rows, hid = 16, 2048
+    h = _rand((rows, hid), dev, torch.bfloat16, 8)
+    gamma = _rand(hid, dev, torch.bfloat16, 9, 0.02) + 1
+    w = _rand((12288, hid), dev, torch.bfloat16, 10, hid ** -0.5)
+    hs = h.float().view(rows, hid // 16, 16)
+    ssq = (hs * hs).sum(-1).t().contiguous()
+    fused = vlasr.decode_linear(h, w, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
+    xn = vlasr.add_rmsnorm(h.clone(), None, gamma)
+    plain = vlasr.decode_linear(xn, w, epilogue="swiglu")
+    torch.cuda.synchronize()
+    same = (fused == plain).float().mean().item()
+    assert normwise(to_np(fused), to_np(plain)) <= 1e-2 and same > 0.9, same
+
+
+def test_row_stride_and_lm_head_width(dev):
+    rows, hid, vocab = 5, 2048, 59264
+    buf = _rand((rows, 3 * hid), dev, torch.bfloat16, 11)
+    x = buf[:, hid:2 * hid]
+    w = _rand((vocab, hid), dev, torch.bfloat16, 12, hid ** -0.5)
+    y = vlasr.decode_linear(x, w)
+    ref = _r(x.float() @ w.float().t(), torch.bfloat16)
+    torch.cuda.synchronize()
+    assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]
+    assert torch.equal(y.float().argmax(-1), ref.argmax(-1)) or \
+        normwise(to_np(y), to_np(ref)) < 5e-3
+
+
+def test_deterministic(dev):
+    x = _rand((16, 2048), dev, torch.bfloat16, 13)
+    w = _rand((2048, 2048), dev, torch.bfloat16, 14, 2048 ** -0.5)
+    a = vlasr.decode_linear(x, w)
+    b = vlasr.decode_linear(x, w)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_rejects(dev):
+    x = _rand((65, 2048), dev, torch.bfloat16, 15)
+    w = _rand((2048, 2048), dev, torch.bfloat16, 16)
+    with pytest.raises(vlasr.VlasrInputError, match="rows"):
+        vlasr.decode_linear(x, w)
+    with pytest.raises(vlasr.VlasrInputError, match="in place"):
+        vlasr.decode_linear(x[:4], w, epilogue="residual")

@@ -139,3 +139,20 @@ def test_graph_replay_matches_eager_steps(decoders, audio16):
     graphed = dec.generate(audio16, PROMPT, max_new_tokens=12, graphs=True).per_chunk_ids
     torch.cuda.synchronize()
     assert graphed == eager
+
+
+def test_fused_step_matches_cublas_step(decoders, audio16, reference_ids):
+    """The fused decode layers (vl_decode_linear) and the cuBLAS path give the
+    same tokens (teacher forced, fp16), both agreeing with the reference."""
+    dec = decoders[torch.float16]
+    res = {}
+    for fused in (True, False):
+        dec.fused = fused
+        try:
+            r = dec.generate(audio16, PROMPT, max_new_tokens=NEW, forced_ids=reference_ids)
+        finally:
+            dec.fused = True
+        res[fused] = [[i for i, _ in (p.get(c, (None, 0)) for p in r.forced_agreement)]
+                      for c in range(CHUNKS)]
+    torch.cuda.synchronize()
+    assert res[True] == res[False]

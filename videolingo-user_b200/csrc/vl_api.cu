@@ -465,4 +465,60 @@ int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cac
       vl::launch_decode_attention(a, dtype, workspace, static_cast<cudaStream_t>(stream)), op);
 }
 
+int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weight,
+                     const float* ssq_in, int ssq_in_parts, float eps, const void* w, int64_t n,
+                     int64_t k, void* y, int64_t y_row_stride, float* ssq_out, int64_t rows,
+                     int epilogue, int dtype, void* stream) {
+  const char* op = "vl_decode_linear";
+  if (x == nullptr || w == nullptr || y == nullptr)
+    return fail(VL_ERR_INVALID, "%s: null pointer", op);
+  if (dtype != VL_F16 && dtype != VL_BF16)
+    return fail(VL_ERR_INVALID, "%s: unsupported dtype %d (f16 or bf16)", op, dtype);
+  if (epilogue != VL_LINEAR_STORE && epilogue != VL_LINEAR_SWIGLU &&
+      epilogue != VL_LINEAR_RESIDUAL)
+    return fail(VL_ERR_INVALID, "%s: unknown epilogue %d", op, epilogue);
+  if (rows < 0 || rows > VL_LINEAR_MAX_ROWS)
+    return fail(VL_ERR_INVALID, "%s: rows must be in [0, %d]", op, VL_LINEAR_MAX_ROWS);
+  if (k <= 0 || k % 256 != 0 || k > kMaxCols)
+    return fail(VL_ERR_INVALID, "%s: k must be a positive multiple of 256", op);
+  const int64_t align_n = epilogue == VL_LINEAR_SWIGLU ? 32 : 16;
+  if (n <= 0 || n % align_n != 0 || n > (int64_t(1) << 28))
+    return fail(VL_ERR_INVALID, "%s: n must be a positive multiple of %lld", op,
+                static_cast<long long>(align_n));
+  const int64_t out_cols = epilogue == VL_LINEAR_SWIGLU ? n / 2 : n;
+  if (x_row_stride < k || x_row_stride % 8 != 0 || y_row_stride < out_cols)
+    return fail(VL_ERR_INVALID, "%s: bad row strides", op);
+  if (!vl::aligned16(x) || !vl::aligned16(w))
+    return fail(VL_ERR_INVALID, "%s: x and w must be 16-byte aligned", op);
+  if (norm_weight != nullptr) {
+    if (ssq_in == nullptr || ssq_in_parts <= 0)
+      return fail(VL_ERR_INVALID, "%s: the RMSNorm prologue needs ssq_in partial sums", op);
+    if (reinterpret_cast<uintptr_t>(norm_weight) % 4 != 0)
+      return fail(VL_ERR_INVALID, "%s: norm_weight must be 4-byte aligned", op);
+    if (!(eps >= 0.0f) || !std::isfinite(eps))
+      return fail(VL_ERR_INVALID, "%s: eps must be finite and >= 0", op);
+  }
+  if (ssq_out != nullptr && epilogue != VL_LINEAR_RESIDUAL)
+    return fail(VL_ERR_INVALID, "%s: ssq_out is written by the RESIDUAL epilogue only", op);
+  if (rows > 0 && overlaps(x, ((rows - 1) * x_row_stride + k) * 2, y,
+                           ((rows - 1) * y_row_stride + out_cols) * 2))
+    return fail(VL_ERR_INVALID, "%s: x overlaps y", op);
+  vl::LinearArgs a{};
+  a.x = x;
+  a.x_row_stride = x_row_stride;
+  a.norm_weight = norm_weight;
+  a.ssq_in = ssq_in;
+  a.ssq_in_parts = ssq_in_parts;
+  a.eps = eps;
+  a.w = w;
+  a.n = n;
+  a.k = k;
+  a.y = y;
+  a.y_row_stride = y_row_stride;
+  a.ssq_out = ssq_out;
+  a.rows = rows;
+  a.epilogue = epilogue;
+  return exec_status(vl::launch_decode_linear(a, dtype, static_cast<cudaStream_t>(stream)), op);
+}
+
 }  // extern "C"

@@ -96,6 +96,25 @@ size_t decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_
 cudaError_t launch_decode_attention(DecodeAttnArgs args, int dtype, void* workspace,
                                     cudaStream_t stream);
 
+// Decode-step linear layers (vl_linear.cu).
+struct LinearArgs {
+  const void* x;             // [rows][x_row_stride], k used
+  int64_t x_row_stride;
+  const void* norm_weight;   // [k] RMSNorm weight, or nullptr
+  const float* ssq_in;       // [ssq_in_parts][rows] partial sums of squares of x's rows
+  int ssq_in_parts;
+  float eps;
+  const void* w;             // [n][k]
+  int64_t n;
+  int64_t k;
+  void* y;                   // [rows][y_row_stride]
+  int64_t y_row_stride;
+  float* ssq_out;            // RESIDUAL: [n / 16][rows], or nullptr
+  int64_t rows;
+  int epilogue;              // VL_LINEAR_STORE / _SWIGLU / _RESIDUAL
+};
+cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, cudaStream_t stream);
+
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream);

@@ -114,6 +114,7 @@ class TextDecoder:
             })
         self.eos = torch.tensor(self.eos_ids, device=self.device, dtype=torch.int64)
         self._states: dict = {}
+        self.fused = True                # decode steps through vl_decode_linear (<= 64 chunks)
         self.last_timings = (0.0, 0.0)   # (prefill ms, decode-steps ms) of the last graphed call
 
     # ------------------------------------------------------------------
@@ -161,12 +162,21 @@ class TextDecoder:
     def step(self, ids: torch.Tensor, active: torch.Tensor, positions: torch.Tensor,
              k_cache, v_cache, chunk_slots: torch.Tensor, workspace: torch.Tensor):
         """One lockstep decode step for the active chunks: ids [chunks] (int64)
-        are the current tokens, positions [chunks] (int32) their positions."""
+        are the current tokens, positions [chunks] (int32) their positions.
+
+        Up to 64 active chunks run the fused path: per layer vl_decode_linear
+        (RMSNorm prologue + q|k|v), vl_decode_attention, vl_decode_linear (o,
+        residual epilogue), vl_decode_linear (RMSNorm prologue + gate|up +
+        SwiGLU epilogue), vl_decode_linear (down, residual epilogue) - five
+        launches; more chunks run cuBLAS GEMMs between the standalone ops."""
         s = self.shape
         qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
         h = ops.embed_gather(ids.view(-1, 1), self.embed, row_map=active).view(-1, s.hidden)
         pos = positions[active.long()].contiguous()
         start = chunk_slots[active.long()].contiguous()
+        rows = h.shape[0]
+        if self.fused and rows <= ops.LINEAR_MAX_ROWS:
+            return self._step_fused(h, pos, start, k_cache, v_cache, workspace)
         delta = None
         for l, lw in enumerate(self.layer_w):
             y = ops.add_rmsnorm(h, delta, lw["ln1"], eps=s.eps)
@@ -260,6 +270,34 @@ class TextDecoder:
                 break
             st["graph"].replay()
         return out[:max_new_tokens]
+
+    def _step_fused(self, h: torch.Tensor, pos: torch.Tensor, start: torch.Tensor, k_cache,
+                    v_cache, workspace: torch.Tensor):
+        s = self.shape
+        rows = h.shape[0]
+        qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        parts = s.hidden // 16
+        ssq_a = torch.empty(parts, rows, dtype=torch.float32, device=self.device)
+        ssq_b = torch.empty(parts, rows, dtype=torch.float32, device=self.device)
+        for l, lw in enumerate(self.layer_w):
+            if l == 0:      # the embedding rows have no partial sums: normalise them first
+                x = ops.add_rmsnorm(h, None, lw["ln1"], eps=s.eps)
+                qkv = ops.decode_linear(x, lw["qkv_t"].t())
+            else:
+                qkv = ops.decode_linear(h, lw["qkv_t"].t(), norm_weight=lw["ln1"], ssq_in=ssq_a,
+                                        eps=s.eps)
+            a = ops.decode_attention(qkv[:, :qw], k_cache[l], v_cache[l], pos, start,
+                                     n_kv_heads=s.kv_heads, head_dim=s.head_dim,
+                                     max_seq_len=self.max_seq_len, k=qkv[:, qw:qw + kw],
+                                     v=qkv[:, qw + kw:], rotary_dim=s.head_dim,
+                                     rope_base=s.rope_base, workspace=workspace)
+            ops.decode_linear(a, lw["o_t"].t(), epilogue="residual", out=h, ssq_out=ssq_b)
+            m = ops.decode_linear(h, lw["gu_t"].t(), norm_weight=lw["ln2"], ssq_in=ssq_b,
+                                  eps=s.eps, epilogue="swiglu")
+            ops.decode_linear(m, lw["down_t"].t(), epilogue="residual", out=h, ssq_out=ssq_a)
+        logits = ops.decode_linear(h, self.lm_head_t.t(), norm_weight=self.norm_w, ssq_in=ssq_a,
+                                   eps=s.eps).float()
+        return logits.argmax(-1), logits
 
     def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,
                  forced_ids: list | None = None, graphs: bool = True) -> DecodeResult:

@@ -397,6 +397,67 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
 
 
 # ---------------------------------------------------------------------------
+# Decode-step linear layers
+# ---------------------------------------------------------------------------
+
+LINEAR_EPILOGUES = {"store": 0, "swiglu": 1, "residual": 2}
+LINEAR_MAX_ROWS = 64
+
+
+def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
+                  out: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
+                  ssq_in: torch.Tensor | None = None, eps: float = 1e-5,
+                  ssq_out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T for at most 64 token rows (vl_decode_linear).
+
+    x [rows, k] (a row stride is allowed), w [n, k].  epilogue "store" -> out
+    [rows, n]; "swiglu" (w = [gate; up]) -> out [rows, n/2]; "residual" ->
+    out is the residual stream [rows, n], updated in place, and ssq_out
+    (float32 [n/16, rows]) receives its per-16-column sums of squares.
+    norm_weight + ssq_in (float32 [parts, rows], such partial sums) apply
+    the RMSNorm prologue to x."""
+    if epilogue not in LINEAR_EPILOGUES:
+        raise VlasrInputError(f"epilogue must be one of {sorted(LINEAR_EPILOGUES)}")
+    _cuda(x, "x")
+    _contig(w, "w")
+    _same(x, w, "w")
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise VlasrInputError("x must be a 2-D tensor with contiguous rows")
+    rows, k = x.shape
+    n = w.shape[0]
+    if w.dim() != 2 or w.shape[1] != k:
+        raise VlasrInputError("w must be [n, k] with x's k")
+    cols = n // 2 if epilogue == "swiglu" else n
+    if epilogue == "residual":
+        if out is None:
+            raise VlasrInputError("the residual epilogue updates `out` in place: pass it")
+    elif out is None:
+        out = torch.empty((rows, cols), dtype=x.dtype, device=x.device)
+    _cuda(out, "out")
+    _same(x, out, "out")
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape != (rows, cols):
+        raise VlasrInputError(f"out must be [{rows}, {cols}] with contiguous rows")
+    parts = 0
+    if norm_weight is not None:
+        _contig(norm_weight, "norm_weight")
+        _same(x, norm_weight, "norm_weight")
+        if ssq_in is None or ssq_in.dtype != torch.float32 or ssq_in.dim() != 2 \
+                or ssq_in.shape[1] != rows:
+            raise VlasrInputError("the RMSNorm prologue needs ssq_in float32 [parts, rows]")
+        _contig(ssq_in, "ssq_in")
+        parts = ssq_in.shape[0]
+    if ssq_out is not None:
+        _contig(ssq_out, "ssq_out")
+        if ssq_out.dtype != torch.float32 or ssq_out.shape != (n // 16, rows):
+            raise VlasrInputError(f"ssq_out must be float32 [{n // 16}, {rows}]")
+    check(_lib.load().vl_decode_linear(
+        _ptr(x), x.stride(0), _ptr(norm_weight), _ptr(ssq_in), parts, float(eps), _ptr(w), n, k,
+        _ptr(out), out.stride(0), _ptr(ssq_out), rows, LINEAR_EPILOGUES[epilogue],
+        _dtype_code(x), _stream(x)), "vl_decode_linear")
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Index ops
 # ---------------------------------------------------------------------------
 
