@@ -124,3 +124,42 @@ def test_host_pipeline_groups_tile_the_chunks(chunks, groups):
     if len(b) > 2:  # half-size first and last groups
         assert b[0][1] - b[0][0] <= b[1][1] - b[1][0]
         assert b[-1][1] - b[-1][0] <= b[-2][1] - b[-2][0]
+
+
+class _ContentEngine:
+    """Fake engine: chunk c (filled with the value c) decodes to [c, c+1000]."""
+
+    def transcribe_ids(self, chunks, prompt_ids, max_new_tokens=256):
+        return [[int(round(float(c[0]))), int(round(float(c[0]))) + 1000] for c in chunks]
+
+
+def _sharded_worker(rank, world, port, chunks, q):
+    try:
+        import numpy as np
+        from vlasr.engine import transcribe_ids_sharded
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=30))
+        pcm = np.repeat(np.arange(chunks, dtype=np.float32)[:, None], 480000, axis=1)
+        ids = transcribe_ids_sharded(_ContentEngine(), pcm, [1, 2, 3], 8)
+        dist.destroy_process_group()
+        q.put((rank, ids == [[c, c + 1000] for c in range(chunks)], None))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, False, repr(exc)))
+
+
+@pytest.mark.parametrize("chunks", [5, 2, 1])
+def test_sharded_engine_returns_every_chunk_in_order(chunks):
+    """Chunk sharding of the in-process engine over 2 gloo ranks: equal and
+    uneven shares, and a rank without chunks."""
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, chunks, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in results), results

@@ -128,11 +128,14 @@ class VlasrAsrBackend:
                  None skips word alignment: every segment spans its chunk
     language_resolver  callable(configured, texts) -> language code
     audio_loader callable(path) -> mono f32 16 kHz PCM (default ffmpeg)
+    group        a torch.distributed process group: every rank runs the same
+                 call; the chunks are sharded over the ranks (one GPU each)
+                 and every rank returns the whole transcription
     """
 
     def __init__(self, model_dir=None, *, engine=None, processor=None, aligner=None,
                  language_resolver=None, audio_loader=None, chunk_seconds: float = 30.0,
-                 max_new_tokens: int = 256, aligner_batch: int = 4):
+                 max_new_tokens: int = 256, aligner_batch: int = 4, group=None):
         self.model_dir = Path(model_dir) if model_dir is not None else None
         self.engine = engine
         self.processor = processor
@@ -142,6 +145,7 @@ class VlasrAsrBackend:
         self.chunk_seconds = float(chunk_seconds)
         self.max_new_tokens = int(max_new_tokens)
         self.aligner_batch = int(aligner_batch)
+        self.group = group      # a torch.distributed group: shard the chunks over its ranks
 
     def _engine(self):
         if self.engine is None:
@@ -176,8 +180,13 @@ class VlasrAsrBackend:
         processor = self._processor()
         prompt_ids = list(processor.apply_transcription_request([arrays[0]]).input_ids[0])
         try:
-            per_chunk = self._engine().transcribe_ids(arrays, prompt_ids,
-                                                      max_new_tokens=self.max_new_tokens)
+            if self.group is not None:
+                from .engine import transcribe_ids_sharded
+                per_chunk = transcribe_ids_sharded(self._engine(), arrays, prompt_ids,
+                                                   self.max_new_tokens, group=self.group)
+            else:
+                per_chunk = self._engine().transcribe_ids(arrays, prompt_ids,
+                                                          max_new_tokens=self.max_new_tokens)
         except StageError:
             raise
         except Exception as exc:  # noqa: BLE001 - engine failures become stage errors

@@ -95,3 +95,31 @@ class AsrEngine:
         self.timings = EngineTimings(ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
                                      ev[2].elapsed_time(ev[3]), *self.decoder.last_timings)
         return result.per_chunk_ids
+
+
+def transcribe_ids_sharded(engine, pcm_chunks, prompt_ids, max_new_tokens: int = 256,
+                           group=None) -> list[list[int]]:
+    """Multi-GPU engine call: one process per GPU, chunks sharded by
+    contiguous range over the ranks of `group` (the partition of the
+    benchmark chain, vlasr.pipeline.shard_range); every rank runs its shard
+    on its own engine and the id lists are all-gathered, so every rank
+    returns the ids of all chunks in chunk order.  Chunks are independent
+    (per-chunk mel normalisation, unmasked per-chunk encoder attention,
+    per-chunk decode), so the ids equal a single-GPU call's."""
+    import torch.distributed as dist
+    from .pipeline import shard_range
+    chunks_np = pcm_chunks if np.asarray(pcm_chunks).ndim == 2 else pad_to_chunks(pcm_chunks)
+    chunks = chunks_np.shape[0]
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    c0, c1 = shard_range(chunks, rank, world)
+    mine = engine.transcribe_ids(chunks_np[c0:c1], prompt_ids,
+                                 max_new_tokens=max_new_tokens) if c1 > c0 else []
+    gathered: list = [None] * world
+    dist.all_gather_object(gathered, mine, group=group)
+    out: list[list[int]] = []
+    for part in gathered:
+        out.extend(part)
+    if len(out) != chunks:
+        raise VlasrInputError(f"sharded engine returned {len(out)} transcripts for {chunks} chunks")
+    return out
