@@ -120,3 +120,9 @@ def test_clamp_words_rules():
 def test_pad_to_chunks():
     out = pad_to_chunks(np.ones(480000 + 10, np.float32))
     assert out.shape == (2, 480000) and out[1, 9] == 1 and out[1, 10] == 0
+
+
+def test_collect_ids_stops_at_the_first_eos():
+    from vlasr.decoder import collect_ids
+    rows = [[5, 6, 59253, 59253, 59253], [7, -1, -1, -1, -1], [8, 9, 10, 11, 12], [59246, 1, 2]]
+    assert collect_ids(rows) == [[5, 6, 59253], [7], [8, 9, 10, 11, 12], [59246]]

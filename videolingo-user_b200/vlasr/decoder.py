@@ -375,16 +375,21 @@ class TextDecoder:
                             forced_agreement=agreement)
 
     def _collect(self, out: torch.Tensor, chunks: int) -> list[list[int]]:
-        """out [steps, chunks] -> per chunk, the ids through the first EOS."""
-        ids = out.t().tolist()
-        per_chunk = []
-        for c in range(chunks):
-            seq = []
-            for i in ids[c]:
-                if i < 0:
-                    break
-                seq.append(i)
-                if i in self.eos_ids:
-                    break
-            per_chunk.append(seq)
-        return per_chunk
+        return collect_ids(out.t().tolist()[:chunks], self.eos_ids)
+
+
+def collect_ids(rows_per_chunk, eos_ids=EOS_IDS) -> list[list[int]]:
+    """Generated-id rows per chunk (-1 = not generated) -> the ids through
+    the first EOS, as the reference collects them (decoder.cu:1783-1790)."""
+    eos = set(int(e) for e in eos_ids)
+    per_chunk = []
+    for row in rows_per_chunk:
+        seq = []
+        for i in row:
+            if i < 0:
+                break
+            seq.append(int(i))
+            if i in eos:
+                break
+        per_chunk.append(seq)
+    return per_chunk
