@@ -362,7 +362,7 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
  *                              y[row][j] = round(y + round(acc)); if
  *                              ssq_out, ssq_out[(j/16)*rows + row] = sum of
  *                              the squares of the 16 new values j..j+15.
- * Requires k % 256 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y 16-byte
+ * Requires k % 512 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y 16-byte
  * aligned with row strides that are multiples of 8 elements, x not
  * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
  */

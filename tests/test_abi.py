@@ -179,7 +179,7 @@ def test_decode_linear_rejects(lib):
     assert call(dtype=0) == 2 and "dtype" in _err(lib)
     assert call(epi=7) == 2 and "epilogue" in _err(lib)
     assert call(rows=65) == 2 and "rows" in _err(lib)
-    assert call(k=2000, xs=2000) == 2 and "multiple of 256" in _err(lib)
+    assert call(k=2000, xs=2000) == 2 and "multiple of 512" in _err(lib)
     assert call(n=3000) == 2 and "multiple of 16" in _err(lib)
     assert call(n=3056, epi=1, ys=1528) == 2 and "multiple of 32" in _err(lib)
     assert call(xs=2052) == 2 and "strides" in _err(lib)

@@ -479,8 +479,8 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
     return fail(VL_ERR_INVALID, "%s: unknown epilogue %d", op, epilogue);
   if (rows < 0 || rows > VL_LINEAR_MAX_ROWS)
     return fail(VL_ERR_INVALID, "%s: rows must be in [0, %d]", op, VL_LINEAR_MAX_ROWS);
-  if (k <= 0 || k % 256 != 0 || k > kMaxCols)
-    return fail(VL_ERR_INVALID, "%s: k must be a positive multiple of 256", op);
+  if (k <= 0 || k % 512 != 0 || k > kMaxCols)
+    return fail(VL_ERR_INVALID, "%s: k must be a positive multiple of 512", op);
   const int64_t align_n = epilogue == VL_LINEAR_SWIGLU ? 32 : 16;
   if (n <= 0 || n % align_n != 0 || n > (int64_t(1) << 28))
     return fail(VL_ERR_INVALID, "%s: n must be a positive multiple of %lld", op,

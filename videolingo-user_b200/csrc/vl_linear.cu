@@ -10,11 +10,12 @@
 // silu_mul_kernel (:103-109, g = half(g / (1 + __expf(-g)) * u)).
 //
 // At decode the token rows are few, so the GEMM is a weight stream: every
-// weight is read once and used M times.  One CTA of 4 warps owns 16 output
-// columns (16 rows of W; 16 gate + 16 up rows for the SwiGLU epilogue); each
-// warp takes a quarter of K and streams its slice of those W rows, and of
-// the x rows, through a private 3-stage cp.async ring of 64-wide k chunks
-// (XOR-swizzled rows, warp-level waits only: no block barrier in the loop).
+// weight is read once and used M times.  One CTA owns 16 output columns (16
+// rows of W with 8 warps; 16 gate + 16 up rows with 4 warps for the SwiGLU
+// epilogue); each warp takes an equal slice of K and streams its part of
+// those W rows, and of the x rows, through a private 3-stage cp.async ring
+// of 64-wide k chunks (XOR-swizzled rows, warp-level waits only: no block
+// barrier in the loop).
 // The products run on the tensor cores (mma.sync m16n8k16, fp32
 // accumulate): A = x rows from ldmatrix, B = W rows from ldmatrix.  The four
 // warps' partial sums meet in shared memory for the epilogue:
@@ -34,8 +35,11 @@
 namespace vl {
 namespace {
 
-constexpr int kLinThreads = 128;
-constexpr int kLinWarps = kLinThreads / 32;
+// Warps per CTA: 8 for the 16-row weight tiles (more bytes in flight per
+// SM), 4 for the 32-row gate|up tiles of the SwiGLU epilogue (whose larger
+// ring would otherwise leave one CTA per SM).
+template <int EPI>
+constexpr int lin_warps() { return EPI == VL_LINEAR_SWIGLU ? 4 : 8; }
 #ifndef VL_LINEAR_STAGES
 #define VL_LINEAR_STAGES 3
 #endif
@@ -112,7 +116,7 @@ __device__ __forceinline__ int lin_swz(int r, int c) { return r * kKc + ((c ^ (r
 template <int MT, int EPI>
 constexpr int lin_stages() {
   constexpr int ntw = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;
-  constexpr size_t per_stage = static_cast<size_t>(kLinWarps) * (ntw + 16 * MT) * kKc * 2;
+  constexpr size_t per_stage = static_cast<size_t>(lin_warps<EPI>()) * (ntw + 16 * MT) * kKc * 2;
   constexpr int fit = static_cast<int>(kLinRingBudget / per_stage);
   return fit < VL_LINEAR_STAGES ? (fit < 2 ? 2 : fit) : VL_LINEAR_STAGES;
 }
@@ -120,12 +124,14 @@ constexpr int lin_stages() {
 template <int MT, int EPI>
 constexpr size_t lin_ring_bytes() {
   constexpr int ntw = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;
-  return static_cast<size_t>(kLinWarps) * lin_stages<MT, EPI>() * (ntw + 16 * MT) * kKc * 2;
+  return static_cast<size_t>(lin_warps<EPI>()) * lin_stages<MT, EPI>() * (ntw + 16 * MT) * kKc * 2;
 }
 
 template <typename T, int MT, int EPI, bool NORM>
-__global__ void __launch_bounds__(kLinThreads)
+__global__ void __launch_bounds__(lin_warps<EPI>() * 32)
     decode_linear_kernel(const __grid_constant__ LinearArgs a) {
+  constexpr int kLinWarps = lin_warps<EPI>();
+  constexpr int kLinThreads = kLinWarps * 32;
   using S = Storage<T>;
   constexpr int NTW = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;  // W rows per CTA
   constexpr int MR = 16 * MT;                                          // x rows (padded)
@@ -145,15 +151,6 @@ __global__ void __launch_bounds__(kLinThreads)
   T* my = ring + warp * kStages * ST_EL;
   const T* x = static_cast<const T*>(a.x);
   const T* w = static_cast<const T*>(a.w);
-
-  if (NORM) {
-    if (tid < a.rows) {
-      float ssq = 0.0f;
-      for (int p = 0; p < a.ssq_in_parts; ++p) ssq += a.ssq_in[static_cast<int64_t>(p) * a.rows + tid];
-      inv_s[tid] = rsqrtf(ssq / static_cast<float>(a.k) + a.eps);
-    }
-    __syncthreads();
-  }
 
   auto issue = [&](int c) {
     T* st = my + (c % kStages) * ST_EL;
@@ -178,6 +175,20 @@ __global__ void __launch_bounds__(kLinThreads)
   for (int s = 0; s < kStages - 1; ++s) {
     if (s < nchunks) issue(s);
     lin_commit();
+  }
+
+  if (NORM) {
+    // with the first weight tiles in flight: a warp per row, lane l sums the
+    // partials l, l+32, ... in order, then a fixed xor tree (deterministic)
+    for (int r = warp; r < a.rows; r += kLinWarps) {
+      float ssq = 0.0f;
+      for (int p = lane; p < a.ssq_in_parts; p += 32)
+        ssq += a.ssq_in[static_cast<int64_t>(p) * a.rows + r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+      if (lane == 0) inv_s[r] = rsqrtf(ssq / static_cast<float>(a.k) + a.eps);
+    }
+    __syncthreads();
   }
 
   float acc[MT][NTW / 8][4];
@@ -295,6 +306,9 @@ __global__ void __launch_bounds__(kLinThreads)
 template <typename T, int MT, int EPI, bool NORM>
 cudaError_t linear_launch(const LinearArgs& a, cudaStream_t stream) {
   constexpr size_t smem = lin_ring_bytes<MT, EPI>() + (64 + 64 * kCols) * sizeof(float);
+  static_assert(static_cast<size_t>(lin_warps<EPI>()) * 16 * MT * (EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols) * 4 <=
+                    lin_ring_bytes<MT, EPI>(),
+                "the cross-warp sums must fit in the ring");
   static_assert(smem <= 227 * 1024, "decode linear shared memory");
   auto kernel = decode_linear_kernel<T, MT, EPI, NORM>;
   if (smem > 48 * 1024) {
@@ -310,7 +324,7 @@ cudaError_t linear_launch(const LinearArgs& a, cudaStream_t stream) {
     }
   }
   const int64_t cols = a.epilogue == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
-  kernel<<<static_cast<unsigned>(cols / kCols), kLinThreads, smem, stream>>>(a);
+  kernel<<<static_cast<unsigned>(cols / kCols), lin_warps<EPI>() * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
