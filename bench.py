@@ -77,6 +77,10 @@ def parse() -> argparse.Namespace:
                         "the reference engine's mel + run_encode_batched + run_decode_batched")
     p.add_argument("--asr-chunks", type=int, default=16, help="30 s chunks per engine call")
     p.add_argument("--asr-tokens", type=int, default=64, help="token budget per chunk")
+    p.add_argument("--linear", action="store_true",
+                   help="decode-layer mode: per-launch graph times of the fused decode "
+                        "projections (vl_decode_linear) beside cuBLAS, and the decode-step "
+                        "graph replay of both paths, at --asr-chunks token rows")
     p.add_argument("--op", default=None,
                    help="profiling mode: run only this op of the per-op table "
                         "(warmup + steps launches, no flush) and print its timing")
@@ -342,6 +346,27 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
                                                head_dim=128, max_seq_len=4096, k=k, v=v,
                                                rotary_dim=128, out=out))
 
+    def _decode_linear(kind):
+        # one 16-row decode projection of the text decoder (hidden 2048, ffn 6144)
+        rows, hid, ffn = 16, 2048, 6144
+        n, k = {"qkv_norm": (3072, hid), "gu_swiglu": (2 * ffn, hid),
+                "o_residual": (hid, hid), "down_residual": (hid, ffn)}[kind]
+        x, w = rnd((rows, k)), rnd((n, k), 0.0, k ** -0.5)
+        gam = rnd(k, 1.0, 0.02)
+        ssq = (x.float() ** 2).view(rows, k // 16, 16).sum(-1).t().contiguous()
+        part = torch.empty(n // 16, rows, dtype=torch.float32, device=dev)
+        out = torch.empty(rows, n // 2 if kind == "gu_swiglu" else n, dtype=bf, device=dev)
+        nbytes = w.numel() * 2 + x.numel() * 2 + out.numel() * 2 * (2 if "residual" in kind else 1)
+        if kind == "qkv_norm":
+            fn = lambda: vlasr.decode_linear(x, w, norm_weight=gam, ssq_in=ssq, out=out)  # noqa: E731
+        elif kind == "gu_swiglu":
+            fn = lambda: vlasr.decode_linear(x, w, norm_weight=gam, ssq_in=ssq,  # noqa: E731
+                                             epilogue="swiglu", out=out)
+        else:
+            fn = lambda: vlasr.decode_linear(x, w, epilogue="residual", out=out,  # noqa: E731
+                                             ssq_out=part)
+        return f"{rows} rows x W [{n},{k}] bf16 ({kind})", nbytes, fn
+
     table = [  # name, builder, iterations, latency-bound
         ("add_layernorm", add_layernorm, 20, False),
         ("gelu_erf", gelu_erf, 20, False),
@@ -357,6 +382,10 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         ("decode_rope_kv_append", decode_rope_kv_append, 20, True),
         ("decode_attention", decode_attention, 20, False),
         ("decode_step_fused", decode_step_fused, 20, False),
+        ("decode_linear_qkv_norm", lambda: _decode_linear("qkv_norm"), 20, False),
+        ("decode_linear_gu_swiglu", lambda: _decode_linear("gu_swiglu"), 20, False),
+        ("decode_linear_o_residual", lambda: _decode_linear("o_residual"), 20, False),
+        ("decode_linear_down_residual", lambda: _decode_linear("down_residual"), 20, False),
     ]
     rows = {}
     for name, build, iters, latency in table:
@@ -580,6 +609,127 @@ ASR_METRIC = "engine audio-seconds/s (log-mel + audio tower + projector + greedy
 ASR_PROMPT = [151, 2222, 3333] + [59260] * 375 + [4444, 5555, 6666, 77]
 
 
+def run_linear_bench(args) -> None:
+    """One GPU: the text decoder's four projections at `--asr-chunks` token
+    rows, each captured 28 times in one CUDA graph over 28 distinct weight
+    matrices (more than L2 holds, as in a decode step) and replayed; device
+    time per launch by CUDA events, for vl_decode_linear with its fused
+    prologue / epilogue and for the bare cuBLAS GEMM (torch.mm) of the same
+    shape.  Then the whole decode step (28 layers + lm_head, graph replay)
+    through both paths of vlasr.decoder.TextDecoder on seeded random weights
+    of the official shapes."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+    import vlasr
+    from vlasr import ops
+    from vlasr.checkpoint import AsrModelConfig, expected_tensors
+    from vlasr.decoder import TextDecoder
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "--linear times this repository's decode layers only"}), flush=True)
+        return
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    vlasr.load()
+    layers, rows, reps = 28, args.asr_chunks, max(args.steps, 1)
+    if not 1 <= rows <= ops.LINEAR_MAX_ROWS:
+        raise SystemExit(f"--asr-chunks must be in 1..{ops.LINEAR_MAX_ROWS} for --linear")
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def mats(n, k):
+        return (torch.randn(layers, n, k, device=dev, generator=g) * k ** -0.5).bfloat16()
+
+    def act(*shape):
+        return torch.randn(*shape, device=dev, generator=g).bfloat16()
+
+    w_qkv, w_o, w_gu, w_d = mats(3072, 2048), mats(2048, 2048), mats(12288, 2048), mats(2048, 6144)
+    gam = (1 + 0.02 * torch.randn(2048, device=dev, generator=g)).bfloat16()
+    h, x, m = act(rows, 2048), act(rows, 2048), act(rows, 6144)
+    ssq = (h.float() ** 2).view(rows, 128, 16).sum(-1).t().contiguous()
+    part = torch.empty(128, rows, dtype=torch.float32, device=dev)
+    y_qkv, y_gu, y_o = act(rows, 3072), act(rows, 6144), act(rows, 2048)
+    y_gu_full = act(rows, 12288)
+
+    def graph_us(body):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            body()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for _ in range(args.warmup):
+            graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del graph
+        return round(a.elapsed_time(b) / reps / layers * 1e3, 2)
+
+    L = range(layers)
+    fused = {
+        "qkv_norm": graph_us(lambda: [ops.decode_linear(h, w_qkv[i], norm_weight=gam, ssq_in=ssq,
+                                                        out=y_qkv) for i in L]),
+        "o_residual": graph_us(lambda: [ops.decode_linear(x, w_o[i], epilogue="residual", out=h,
+                                                          ssq_out=part) for i in L]),
+        "gu_norm_swiglu": graph_us(lambda: [ops.decode_linear(h, w_gu[i], norm_weight=gam,
+                                                              ssq_in=ssq, epilogue="swiglu",
+                                                              out=y_gu) for i in L]),
+        "down_residual": graph_us(lambda: [ops.decode_linear(m, w_d[i], epilogue="residual",
+                                                             out=h, ssq_out=part) for i in L]),
+    }
+    cublas = {
+        "qkv": graph_us(lambda: [torch.mm(h, w_qkv[i].t(), out=y_qkv) for i in L]),
+        "o": graph_us(lambda: [torch.mm(x, w_o[i].t(), out=y_o) for i in L]),
+        "gu": graph_us(lambda: [torch.mm(h, w_gu[i].t(), out=y_gu_full) for i in L]),
+        "down": graph_us(lambda: [torch.mm(m, w_d[i].t(), out=y_o) for i in L]),
+    }
+    mb = {"qkv": 3072 * 2048 * 2 / 1e6, "o": 2048 * 2048 * 2 / 1e6,
+          "gu": 12288 * 2048 * 2 / 1e6, "down": 2048 * 6144 * 2 / 1e6}
+    del w_qkv, w_o, w_gu, w_d
+    torch.cuda.empty_cache()
+
+    weights = {}
+    for name, shape in expected_tensors(AsrModelConfig()):
+        if not name.startswith("language_model."):
+            continue
+        t = torch.randn(shape, device=dev, generator=g)
+        if "norm" in name:
+            t = 1 + 0.02 * t
+        elif "embed" in name:
+            t = t * 0.02
+        else:
+            t = t * shape[-1] ** -0.5
+        weights[name] = t.bfloat16()
+    dec = TextDecoder(weights)
+    del weights
+    audio = act(rows * 375, 2048)
+    replay = {}
+    for path in ("fused", "cublas"):
+        dec.fused = path == "fused"
+        dec._states.clear()
+        dec.generate(audio, ASR_PROMPT, max_new_tokens=2)
+        dec.replay_step(rows, args.warmup)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        dec.replay_step(rows, reps)
+        b.record()
+        torch.cuda.synchronize()
+        replay[path] = round(a.elapsed_time(b) / reps * 1e3, 1)
+    print(json.dumps({"mode": "decode_linear", "rows": rows, "layers": layers, "reps": reps,
+                      "us_per_launch_fused": fused, "us_per_launch_cublas": cublas,
+                      "weight_mb": {k: round(v, 1) for k, v in mb.items()},
+                      "decode_step_replay_us": replay}), flush=True)
+
+
 def run_asr_bench(args) -> None:
     """One GPU: the whole engine call on `--asr-chunks` chunks of host PCM with
     a `--asr-tokens` budget, as the reference CLI's transcribe runs it
@@ -732,6 +882,9 @@ def main() -> None:
     args = parse()
     if args.encoder:
         run_encoder_bench(args)
+        return
+    if args.linear:
+        run_linear_bench(args)
         return
     if args.asr:
         run_asr_bench(args)

@@ -295,6 +295,27 @@ VL_EXPORT int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache,
                       int dtype, int32_t* status, void* stream);
 
 /*
+ * Launch flags of the decode-step entry points (vl_decode_attention,
+ * vl_decode_linear).
+ *
+ * VL_LAUNCH_PDL  launch as a programmatic dependent of the kernel before it
+ *                in the stream: the new kernel's blocks may start while that
+ *                kernel finishes and prefetch inputs it cannot be writing,
+ *                and they wait for its completion (and its writes) before
+ *                reading anything else.  The caller guarantees that the
+ *                kernel before it in the stream writes none of:
+ *                  vl_decode_linear     w, norm_weight;
+ *                  vl_decode_attention  positions, seq_start and, with k / v
+ *                                       given, the cache rows before each
+ *                                       token's position.
+ *                Results are identical with and without the flag.  In a
+ *                chain of such launches (a decode step captured in a CUDA
+ *                graph) each kernel's weight or cache stream overlaps the
+ *                tail of the kernel before it.
+ */
+#define VL_LAUNCH_PDL 1
+
+/*
  * Decode-step attention: one query token per sequence against its KV cache,
  * grouped-query heads (n_q_heads / n_kv_heads query heads share a kv head),
  * optionally fused with the RoPE of q and k at the token's position and the
@@ -325,6 +346,7 @@ VL_EXPORT int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache,
  * workspace: vl_decode_attention_workspace_bytes(...) bytes, zero-filled
  * before its first use; every call leaves it zero-filled again (the split
  * counters reset themselves), so one workspace serves calls in stream order.
+ * flags: 0 or VL_LAUNCH_PDL.
  */
 #define VL_DECODE_MAX_SEQ_LEN 262144
 
@@ -340,7 +362,8 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
                                   int64_t kv_row_stride, int64_t cache_row_stride,
                                   int64_t max_seq_len, int64_t num_slots, void* out,
                                   int64_t out_row_stride, int dtype, void* workspace,
-                                  size_t workspace_bytes, int32_t* status, void* stream);
+                                  size_t workspace_bytes, int32_t* status, int flags,
+                                  void* stream);
 
 /*
  * Decode-step linear layer: y = x W^T for rows <= 64 token rows (W [n][k]
@@ -362,9 +385,10 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
  *                              y[row][j] = round(y + round(acc)); if
  *                              ssq_out, ssq_out[(j/16)*rows + row] = sum of
  *                              the squares of the 16 new values j..j+15.
- * Requires k % 512 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y 16-byte
- * aligned with row strides that are multiples of 8 elements, x not
+ * Requires k % 512 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y and
+ * norm_weight 16-byte aligned with row strides that are multiples of 8 elements, x not
  * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
+ * flags: 0 or VL_LAUNCH_PDL.
  */
 #define VL_LINEAR_STORE 0
 #define VL_LINEAR_SWIGLU 1
@@ -375,7 +399,7 @@ VL_EXPORT int vl_decode_linear(const void* x, int64_t x_row_stride, const void* 
                                const float* ssq_in, int ssq_in_parts, float eps,
                                const void* w, int64_t n, int64_t k, void* y,
                                int64_t y_row_stride, float* ssq_out, int64_t rows,
-                               int epilogue, int dtype, void* stream);
+                               int epilogue, int dtype, int flags, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -143,10 +143,10 @@ def test_decode_attention_rejects(lib):
     def call(q=FAKE, k=None, v=None, kc=FAKE * 2, vc=FAKE * 3, pos=FAKE * 4, st=FAKE * 5,
              tokens=4, nq=16, nkv=4, hd=128, rot=0, base=10000.0, scale=0.0, qs=2048, ks=512,
              cs=512, max_len=1024, slots=4096, out=FAKE * 6, os_=2048, dtype=2, ws=FAKE * 7,
-             ws_bytes=1 << 30):
+             ws_bytes=1 << 30, flags=0):
         return lib.vl_decode_attention(q, k, v, kc, vc, pos, st, tokens, nq, nkv, hd, rot, base,
                                        scale, qs, ks, cs, max_len, slots, out, os_, dtype, ws,
-                                       ws_bytes, None, None)
+                                       ws_bytes, None, flags, None)
 
     assert call(q=None) == 2 and "null" in _err(lib)
     assert call(k=FAKE * 8) == 2 and "both" in _err(lib)
@@ -164,6 +164,7 @@ def test_decode_attention_rejects(lib):
     assert call(ws_bytes=16) == 2 and "workspace" in _err(lib)
     assert call(out=FAKE * 2) == 2 and "overlaps" in _err(lib)
     assert call(scale=float("nan")) == 2 and "scale" in _err(lib)
+    assert call(flags=2) == 2 and "flags" in _err(lib)
     assert lib.vl_decode_attention_workspace_bytes(64, 16, 4, 128, 4096) >= 64 * 4 * 4
     assert lib.vl_decode_attention_workspace_bytes(0, 16, 4, 128, 4096) == 0
     assert lib.vl_decode_attention_workspace_bytes(1, 16, 3, 128, 4096) == 0
@@ -171,9 +172,9 @@ def test_decode_attention_rejects(lib):
 
 def test_decode_linear_rejects(lib):
     def call(x=FAKE, xs=2048, g=None, ssq=None, parts=0, eps=1e-5, w=FAKE * 2, n=3072, k=2048,
-             y=FAKE * 1000, ys=3072, so=None, rows=16, epi=0, dtype=2):
+             y=FAKE * 1000, ys=3072, so=None, rows=16, epi=0, dtype=2, flags=0):
         return lib.vl_decode_linear(x, xs, g, ssq, parts, eps, w, n, k, y, ys, so, rows, epi,
-                                    dtype, None)
+                                    dtype, flags, None)
 
     assert call(x=None) == 2 and "null" in _err(lib)
     assert call(dtype=0) == 2 and "dtype" in _err(lib)
@@ -187,6 +188,8 @@ def test_decode_linear_rejects(lib):
     assert call(g=FAKE * 3) == 2 and "ssq_in" in _err(lib)
     assert call(so=FAKE * 4) == 2 and "RESIDUAL" in _err(lib)
     assert call(y=FAKE) == 2 and "overlaps" in _err(lib)
+    assert call(flags=4) == 2 and "flags" in _err(lib)
+    assert call(g=FAKE * 3 + 4, ssq=FAKE * 4, parts=128) == 2 and "norm_weight" in _err(lib)
 
 
 def test_error_is_thread_local(lib):

@@ -128,3 +128,59 @@ def test_rejects(dev):
         vlasr.decode_linear(x, w)
     with pytest.raises(vlasr.VlasrInputError, match="in place"):
         vlasr.decode_linear(x[:4], w, epilogue="residual")
+
+
+def test_pdl_chain_is_bit_identical(dev):
+    """VL_LAUNCH_PDL: a decode-layer chain (down + residual -> RMSNorm + q|k|v
+    -> RoPE + append + attention -> o + residual -> RMSNorm + gate|up +
+    SwiGLU) launched as programmatic dependents gives the same bits as
+    ordinary launches, eagerly and replayed from a CUDA graph."""
+    rows, hid, ffn, slots = 16, 2048, 6144, 1024
+    w_d = _rand((hid, ffn), dev, torch.bfloat16, 20, ffn ** -0.5)
+    w_qkv = _rand((3072, hid), dev, torch.bfloat16, 21, hid ** -0.5)
+    w_o = _rand((hid, hid), dev, torch.bfloat16, 22, hid ** -0.5)
+    w_gu = _rand((2 * ffn, hid), dev, torch.bfloat16, 23, hid ** -0.5)
+    g1 = _rand(hid, dev, torch.bfloat16, 24, 0.02) + 1
+    g2 = _rand(hid, dev, torch.bfloat16, 25, 0.02) + 1
+    h0 = _rand((rows, hid), dev, torch.bfloat16, 26)
+    m0 = _rand((rows, ffn), dev, torch.bfloat16, 27)
+    kc0 = _rand((rows * slots, 512), dev, torch.bfloat16, 28)
+    vc0 = _rand((rows * slots, 512), dev, torch.bfloat16, 29)
+    pos = torch.randint(0, 600, (rows,), generator=torch.Generator().manual_seed(30)).to(
+        dev, torch.int32)
+    start = torch.arange(rows, device=dev, dtype=torch.int64) * slots
+
+    def state():
+        return {"h": h0.clone(), "kc": kc0.clone(), "vc": vc0.clone(),
+                "sa": torch.empty(128, rows, device=dev), "sb": torch.empty(128, rows, device=dev),
+                "ws": torch.zeros(vlasr.decode_attention_workspace_bytes(rows, 16, 4, 128, slots),
+                                  dtype=torch.uint8, device=dev),
+                "m": torch.empty(rows, ffn, dtype=torch.bfloat16, device=dev)}
+
+    def chain(st, pdl):
+        vlasr.decode_linear(m0, w_d, epilogue="residual", out=st["h"], ssq_out=st["sa"], pdl=pdl)
+        qkv = vlasr.decode_linear(st["h"], w_qkv, norm_weight=g1, ssq_in=st["sa"], pdl=pdl)
+        a = vlasr.decode_attention(qkv[:, :2048], st["kc"], st["vc"], pos, start, n_kv_heads=4,
+                                   head_dim=128, max_seq_len=slots, k=qkv[:, 2048:2560],
+                                   v=qkv[:, 2560:], rotary_dim=128, workspace=st["ws"], pdl=pdl)
+        vlasr.decode_linear(a, w_o, epilogue="residual", out=st["h"], ssq_out=st["sb"], pdl=pdl)
+        vlasr.decode_linear(st["h"], w_gu, norm_weight=g2, ssq_in=st["sb"], epilogue="swiglu",
+                            out=st["m"], pdl=pdl)
+
+    plain, eager = state(), state()
+    chain(plain, False)
+    chain(eager, True)
+    graphed = state()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            chain(graphed, True)
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    for key in ("h", "m", "kc", "vc", "sa", "sb"):
+        assert torch.equal(eager[key], plain[key]), key
+        assert torch.equal(graphed[key], plain[key]), key
+    del graph

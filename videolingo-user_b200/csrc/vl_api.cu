@@ -389,7 +389,8 @@ int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cac
                         int rotary_dim, double rope_base, float scale, int64_t q_row_stride,
                         int64_t kv_row_stride, int64_t cache_row_stride, int64_t max_seq_len,
                         int64_t num_slots, void* out, int64_t out_row_stride, int dtype,
-                        void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+                        void* workspace, size_t workspace_bytes, int32_t* status, int flags,
+                        void* stream) {
   const char* op = "vl_decode_attention";
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || positions == nullptr ||
       seq_start == nullptr || out == nullptr)
@@ -398,6 +399,8 @@ int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cac
     return fail(VL_ERR_INVALID, "%s: k and v must both be given or both be null", op);
   if (dtype != VL_F16 && dtype != VL_BF16)
     return fail(VL_ERR_INVALID, "%s: unsupported dtype %d (f16 or bf16)", op, dtype);
+  if ((flags & ~VL_LAUNCH_PDL) != 0)
+    return fail(VL_ERR_INVALID, "%s: unknown flags 0x%x", op, flags);
   if (tokens < 0 || tokens > 0x7fffffff || n_q_heads <= 0 || n_kv_heads <= 0 ||
       n_kv_heads > 65535 || n_q_heads % n_kv_heads != 0)
     return fail(VL_ERR_INVALID, "%s: bad shape tokens=%lld heads=%d/%d", op,
@@ -462,18 +465,22 @@ int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cac
   a.num_slots = num_slots;
   a.status = status;
   return exec_status(
-      vl::launch_decode_attention(a, dtype, workspace, static_cast<cudaStream_t>(stream)), op);
+      vl::launch_decode_attention(a, dtype, workspace, (flags & VL_LAUNCH_PDL) != 0,
+                                  static_cast<cudaStream_t>(stream)),
+      op);
 }
 
 int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weight,
                      const float* ssq_in, int ssq_in_parts, float eps, const void* w, int64_t n,
                      int64_t k, void* y, int64_t y_row_stride, float* ssq_out, int64_t rows,
-                     int epilogue, int dtype, void* stream) {
+                     int epilogue, int dtype, int flags, void* stream) {
   const char* op = "vl_decode_linear";
   if (x == nullptr || w == nullptr || y == nullptr)
     return fail(VL_ERR_INVALID, "%s: null pointer", op);
   if (dtype != VL_F16 && dtype != VL_BF16)
     return fail(VL_ERR_INVALID, "%s: unsupported dtype %d (f16 or bf16)", op, dtype);
+  if ((flags & ~VL_LAUNCH_PDL) != 0)
+    return fail(VL_ERR_INVALID, "%s: unknown flags 0x%x", op, flags);
   if (epilogue != VL_LINEAR_STORE && epilogue != VL_LINEAR_SWIGLU &&
       epilogue != VL_LINEAR_RESIDUAL)
     return fail(VL_ERR_INVALID, "%s: unknown epilogue %d", op, epilogue);
@@ -493,8 +500,8 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
   if (norm_weight != nullptr) {
     if (ssq_in == nullptr || ssq_in_parts <= 0)
       return fail(VL_ERR_INVALID, "%s: the RMSNorm prologue needs ssq_in partial sums", op);
-    if (reinterpret_cast<uintptr_t>(norm_weight) % 4 != 0)
-      return fail(VL_ERR_INVALID, "%s: norm_weight must be 4-byte aligned", op);
+    if (!vl::aligned16(norm_weight))
+      return fail(VL_ERR_INVALID, "%s: norm_weight must be 16-byte aligned", op);
     if (!(eps >= 0.0f) || !std::isfinite(eps))
       return fail(VL_ERR_INVALID, "%s: eps must be finite and >= 0", op);
   }
@@ -518,7 +525,9 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
   a.ssq_out = ssq_out;
   a.rows = rows;
   a.epilogue = epilogue;
-  return exec_status(vl::launch_decode_linear(a, dtype, static_cast<cudaStream_t>(stream)), op);
+  return exec_status(vl::launch_decode_linear(a, dtype, (flags & VL_LAUNCH_PDL) != 0,
+                                              static_cast<cudaStream_t>(stream)),
+                     op);
 }
 
 }  // extern "C"

@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
   T* out = static_cast<T*>(a.out) + t * a.out_row_stride + static_cast<int64_t>(h) * G * HD;
 
   if (pos < 0 || pos >= a.max_seq_len || start < 0 || start > a.num_slots - 1 - pos) {
+    pdl_wait();
     if (s == 0) {
       for (int i = tid; i < G * HD; i += kAttnThreads) out[i] = S::from_float(0.0f);
       if (tid == 0 && a.status) atomicOr(a.status, VL_STATUS_BAD_SLOT);
@@ -228,11 +229,18 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
       cp_async16(vd + swz<HD>(r, my_chunk), vg + off, ok ? 16 : 0);
     }
   };
+  // With the fused append the cached rows are those before the position,
+  // written by earlier steps: they stream in while the kernel before this
+  // one (which may be producing q and the new k / v rows) finishes.  Without
+  // it the row at the position may have just been appended: wait first.
+  if (!fresh) pdl_wait();
 #pragma unroll
   for (int st = 0; st < kStages - 1; ++st) {
     if (st < ntiles) issue(st);
     cp_async_commit();
   }
+  if (fresh) pdl_wait();
+  pdl_release();
 
   const T* qrow = static_cast<const T*>(a.q) + t * a.q_row_stride + static_cast<int64_t>(h) * G * HD;
   load_row_f32<T>(&sm.q[0][0], qrow, G * HD, tid);
@@ -517,7 +525,7 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
 }
 
 template <typename T, int HD, int G>
-cudaError_t launch_typed(const DecodeAttnArgs& a, cudaStream_t stream) {
+cudaError_t launch_typed(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream) {
   const InvFreq freq = make_inv_freq(a.rope_base, a.rotary_dim);
   constexpr size_t ring = static_cast<size_t>(kStages) * 2 * kTile * HD * sizeof(T);
   constexpr size_t partials = static_cast<size_t>(kAttnWarps) * G * HD * sizeof(float);
@@ -541,23 +549,22 @@ cudaError_t launch_typed(const DecodeAttnArgs& a, cudaStream_t stream) {
   // tokens on x (up to 2^31 - 1), kv heads on y, splits (<= 64) on z
   const dim3 grid(static_cast<unsigned>(a.tokens), static_cast<unsigned>(a.n_kv_heads),
                   static_cast<unsigned>(a.max_splits));
-  kernel<<<grid, kAttnThreads, smem, stream>>>(a, freq);
-  return cudaGetLastError();
+  return launch_kernel(kernel, grid, dim3(kAttnThreads), smem, stream, pdl, a, freq);
 }
 
 template <typename T>
-cudaError_t launch_dtype(const DecodeAttnArgs& a, cudaStream_t stream) {
+cudaError_t launch_dtype(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream) {
   const int G = a.n_q_heads / a.n_kv_heads;
   if (a.head_dim == 128) {
-    if (G == 1) return launch_typed<T, 128, 1>(a, stream);
-    if (G == 2) return launch_typed<T, 128, 2>(a, stream);
-    if (G == 4) return launch_typed<T, 128, 4>(a, stream);
-    if (G == 8) return launch_typed<T, 128, 8>(a, stream);
+    if (G == 1) return launch_typed<T, 128, 1>(a, pdl, stream);
+    if (G == 2) return launch_typed<T, 128, 2>(a, pdl, stream);
+    if (G == 4) return launch_typed<T, 128, 4>(a, pdl, stream);
+    if (G == 8) return launch_typed<T, 128, 8>(a, pdl, stream);
   } else if (a.head_dim == 64) {
-    if (G == 1) return launch_typed<T, 64, 1>(a, stream);
-    if (G == 2) return launch_typed<T, 64, 2>(a, stream);
-    if (G == 4) return launch_typed<T, 64, 4>(a, stream);
-    if (G == 8) return launch_typed<T, 64, 8>(a, stream);
+    if (G == 1) return launch_typed<T, 64, 1>(a, pdl, stream);
+    if (G == 2) return launch_typed<T, 64, 2>(a, pdl, stream);
+    if (G == 4) return launch_typed<T, 64, 4>(a, pdl, stream);
+    if (G == 8) return launch_typed<T, 64, 8>(a, pdl, stream);
   }
   return cudaErrorInvalidValue;
 }
@@ -594,7 +601,7 @@ size_t decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_
   return counters + ((o + 255) & ~size_t(255)) + ml;
 }
 
-cudaError_t launch_decode_attention(DecodeAttnArgs a, int dtype, void* workspace,
+cudaError_t launch_decode_attention(DecodeAttnArgs a, int dtype, void* workspace, bool pdl,
                                     cudaStream_t stream) {
   if (a.tokens == 0) return cudaSuccess;
   a.split = static_cast<int>(decode_attention_split(a.tokens, a.n_kv_heads, a.max_seq_len));
@@ -607,8 +614,8 @@ cudaError_t launch_decode_attention(DecodeAttnArgs a, int dtype, void* workspace
   a.counters = reinterpret_cast<int*>(ws);
   a.o_part = reinterpret_cast<float*>(ws + counters);
   a.ml_part = reinterpret_cast<float2*>(ws + counters + ((o + 255) & ~size_t(255)));
-  if (dtype == kDtypeBF16) return launch_dtype<__nv_bfloat16>(a, stream);
-  if (dtype == kDtypeF16) return launch_dtype<__half>(a, stream);
+  if (dtype == kDtypeBF16) return launch_dtype<__nv_bfloat16>(a, pdl, stream);
+  if (dtype == kDtypeF16) return launch_dtype<__half>(a, pdl, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -139,6 +139,38 @@ __device__ __forceinline__ float warp_max(float v) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream serialization attribute may start while the kernel before it in the
+// stream is still running.  It reads only inputs that kernel cannot be
+// writing until pdl_wait(), which returns once that kernel has completed
+// and its writes are visible (immediately for an ordinary launch), and it
+// calls pdl_release() only after pdl_wait(), so the kernel after it can
+// start early but never before this one's predecessor has completed.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch `kernel`, as a programmatic dependent of the stream's previous
+// kernel when `pdl` is set.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, bool pdl, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Number of SMs of the current device (cached per device id).
 int sm_count();
 

@@ -93,7 +93,9 @@ bool decode_attention_supported(int head_dim, int group);
 int64_t decode_attention_split(int64_t tokens, int n_kv_heads, int64_t max_seq_len);
 size_t decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_heads,
                                         int head_dim, int64_t max_seq_len);
-cudaError_t launch_decode_attention(DecodeAttnArgs args, int dtype, void* workspace,
+// pdl: launch as a programmatic dependent of the stream's previous kernel
+// (VL_LAUNCH_PDL of the C ABI).
+cudaError_t launch_decode_attention(DecodeAttnArgs args, int dtype, void* workspace, bool pdl,
                                     cudaStream_t stream);
 
 // Decode-step linear layers (vl_linear.cu).
@@ -113,7 +115,8 @@ struct LinearArgs {
   int64_t rows;
   int epilogue;              // VL_LINEAR_STORE / _SWIGLU / _RESIDUAL
 };
-cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, cudaStream_t stream);
+cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, bool pdl,
+                                 cudaStream_t stream);
 
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,

@@ -15,9 +15,10 @@
 // epilogue); each warp takes an equal slice of K and streams its part of
 // those W rows, and of the x rows, through a private 3-stage cp.async ring
 // of 64-wide k chunks (XOR-swizzled rows, warp-level waits only: no block
-// barrier in the loop).
+// barrier in the loop).  With the RMSNorm prologue the ring also carries the
+// chunk's 64 norm weights, so the loop makes no dependent global load.
 // The products run on the tensor cores (mma.sync m16n8k16, fp32
-// accumulate): A = x rows from ldmatrix, B = W rows from ldmatrix.  The four
+// accumulate): A = x rows from ldmatrix, B = W rows from ldmatrix.  The
 // warps' partial sums meet in shared memory for the epilogue:
 //   STORE     y = round(acc)
 //   SWIGLU    y = round(silu(round(acc_gate)) * round(acc_up))
@@ -112,19 +113,35 @@ __device__ __forceinline__ uint32_t lin_pack2<__half>(float lo, float hi) {
 // offset (elements) of 16-byte chunk c of a 64-wide tile row r
 __device__ __forceinline__ int lin_swz(int r, int c) { return r * kKc + ((c ^ (r & 7)) << 3); }
 
+// Elements of one ring stage: W rows, x rows (padded to 16 * MT) and, with
+// the RMSNorm prologue, the chunk's norm weights.
+template <int MT, int EPI, bool NORM>
+constexpr int lin_stage_elems() {
+  return ((EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols) + 16 * MT + (NORM ? 1 : 0)) * kKc;
+}
+
 // Ring stages per warp: VL_LINEAR_STAGES, fewer when the ring would not fit.
-template <int MT, int EPI>
+template <int MT, int EPI, bool NORM>
 constexpr int lin_stages() {
-  constexpr int ntw = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;
-  constexpr size_t per_stage = static_cast<size_t>(lin_warps<EPI>()) * (ntw + 16 * MT) * kKc * 2;
+  constexpr size_t per_stage = static_cast<size_t>(lin_warps<EPI>()) * lin_stage_elems<MT, EPI, NORM>() * 2;
   constexpr int fit = static_cast<int>(kLinRingBudget / per_stage);
   return fit < VL_LINEAR_STAGES ? (fit < 2 ? 2 : fit) : VL_LINEAR_STAGES;
 }
 
-template <int MT, int EPI>
+template <int MT, int EPI, bool NORM>
 constexpr size_t lin_ring_bytes() {
-  constexpr int ntw = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;
-  return static_cast<size_t>(lin_warps<EPI>()) * lin_stages<MT, EPI>() * (ntw + 16 * MT) * kKc * 2;
+  return static_cast<size_t>(lin_warps<EPI>()) * lin_stages<MT, EPI, NORM>() *
+         lin_stage_elems<MT, EPI, NORM>() * 2;
+}
+
+// Shared memory after the ring: 64 inverse RMS values, and for the RESIDUAL
+// epilogue the [64][16] new residual values.  Keeping the SwiGLU CTA at
+// about 73 KB lets three of them share an SM, so the 384 gate|up tiles of
+// the decoder run in one wave.
+template <int MT, int EPI, bool NORM>
+constexpr size_t lin_smem_bytes() {
+  return lin_ring_bytes<MT, EPI, NORM>() +
+         (64 + (EPI == VL_LINEAR_RESIDUAL ? 64 * kCols : 0)) * sizeof(float);
 }
 
 template <typename T, int MT, int EPI, bool NORM>
@@ -135,11 +152,11 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
   using S = Storage<T>;
   constexpr int NTW = EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols;  // W rows per CTA
   constexpr int MR = 16 * MT;                                          // x rows (padded)
-  constexpr int W_EL = NTW * kKc, X_EL = MR * kKc, ST_EL = W_EL + X_EL;
-  constexpr int kStages = lin_stages<MT, EPI>();
+  constexpr int W_EL = NTW * kKc, X_EL = MR * kKc, ST_EL = lin_stage_elems<MT, EPI, NORM>();
+  constexpr int kStages = lin_stages<MT, EPI, NORM>();
   extern __shared__ __align__(128) unsigned char smem[];
   T* ring = reinterpret_cast<T*>(smem);
-  float* inv_s = reinterpret_cast<float*>(smem + lin_ring_bytes<MT, EPI>());  // [64]
+  float* inv_s = reinterpret_cast<float*>(smem + lin_ring_bytes<MT, EPI, NORM>());  // [64]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
@@ -151,8 +168,10 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
   T* my = ring + warp * kStages * ST_EL;
   const T* x = static_cast<const T*>(a.x);
   const T* w = static_cast<const T*>(a.w);
+  const T* gam = static_cast<const T*>(a.norm_weight);
 
-  auto issue = [&](int c) {
+  // chunk c: the W rows and norm weights (inputs of the model), then the x rows
+  auto issue_w = [&](int c) {
     T* st = my + (c % kStages) * ST_EL;
     const int64_t kk = kbase + static_cast<int64_t>(c) * kKc;
 #pragma unroll
@@ -163,6 +182,11 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
                                : col0 + r;
       lin_cp16(st + lin_swz(r, ch), w + wrow * a.k + kk + ch * 8, 16);
     }
+    if (NORM && lane < kKc / 8) lin_cp16(st + W_EL + X_EL + lane * 8, gam + kk + lane * 8, 16);
+  };
+  auto issue_x = [&](int c) {
+    T* st = my + (c % kStages) * ST_EL;
+    const int64_t kk = kbase + static_cast<int64_t>(c) * kKc;
 #pragma unroll
     for (int i = lane; i < MR * 8; i += 32) {
       const int r = i >> 3, ch = i & 7;
@@ -171,9 +195,19 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
                ok ? 16 : 0);
     }
   };
+  // The first kStages-1 chunks: their weights in one group, issued before
+  // the wait for the previous kernel (which may still be producing x and the
+  // sums of squares), then their x rows in one group each.  Chunk c's data is
+  // complete with commit group c + 1 before the loop and in it alike.
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s)
+    if (s < nchunks) issue_w(s);
+  lin_commit();
+  pdl_wait();
+  pdl_release();
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
-    if (s < nchunks) issue(s);
+    if (s < nchunks) issue_x(s);
     lin_commit();
   }
 
@@ -199,11 +233,13 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.0f;
 
-  const T* gam = static_cast<const T*>(a.norm_weight);
   for (int c = 0; c < nchunks; ++c) {
     lin_wait<kStages - 2>();
     __syncwarp();  // the chunk is visible to the warp; the stage of chunk c-1 is free
-    if (c + kStages - 1 < nchunks) issue(c + kStages - 1);
+    if (c + kStages - 1 < nchunks) {
+      issue_w(c + kStages - 1);
+      issue_x(c + kStages - 1);
+    }
     lin_commit();
     const T* wt = my + (c % kStages) * ST_EL;
     const T* xt = wt + W_EL;
@@ -224,9 +260,9 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
       }
       uint32_t g01 = 0u, g89 = 0u;
       if (NORM) {
-        const int64_t kg = kbase + static_cast<int64_t>(c) * kKc + ks * 16 + 2 * tig;
-        g01 = __ldg(reinterpret_cast<const unsigned int*>(gam + kg));
-        g89 = __ldg(reinterpret_cast<const unsigned int*>(gam + kg + 8));
+        const T* gt = xt + X_EL + ks * 16 + 2 * tig;
+        g01 = *reinterpret_cast<const uint32_t*>(gt);
+        g89 = *reinterpret_cast<const uint32_t*>(gt + 8);
       }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
@@ -304,10 +340,10 @@ __global__ void __launch_bounds__(lin_warps<EPI>() * 32)
 }
 
 template <typename T, int MT, int EPI, bool NORM>
-cudaError_t linear_launch(const LinearArgs& a, cudaStream_t stream) {
-  constexpr size_t smem = lin_ring_bytes<MT, EPI>() + (64 + 64 * kCols) * sizeof(float);
+cudaError_t linear_launch(const LinearArgs& a, bool pdl, cudaStream_t stream) {
+  constexpr size_t smem = lin_smem_bytes<MT, EPI, NORM>();
   static_assert(static_cast<size_t>(lin_warps<EPI>()) * 16 * MT * (EPI == VL_LINEAR_SWIGLU ? 2 * kCols : kCols) * 4 <=
-                    lin_ring_bytes<MT, EPI>(),
+                    lin_ring_bytes<MT, EPI, NORM>(),
                 "the cross-warp sums must fit in the ring");
   static_assert(smem <= 227 * 1024, "decode linear shared memory");
   auto kernel = decode_linear_kernel<T, MT, EPI, NORM>;
@@ -324,39 +360,39 @@ cudaError_t linear_launch(const LinearArgs& a, cudaStream_t stream) {
     }
   }
   const int64_t cols = a.epilogue == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
-  kernel<<<static_cast<unsigned>(cols / kCols), lin_warps<EPI>() * 32, smem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_kernel(kernel, dim3(static_cast<unsigned>(cols / kCols)),
+                       dim3(lin_warps<EPI>() * 32), smem, stream, pdl, a);
 }
 
 template <typename T, int MT>
-cudaError_t linear_mt(const LinearArgs& a, cudaStream_t stream) {
+cudaError_t linear_mt(const LinearArgs& a, bool pdl, cudaStream_t stream) {
   const bool norm = a.norm_weight != nullptr;
   switch (a.epilogue) {
     case VL_LINEAR_STORE:
-      return norm ? linear_launch<T, MT, VL_LINEAR_STORE, true>(a, stream)
-                  : linear_launch<T, MT, VL_LINEAR_STORE, false>(a, stream);
+      return norm ? linear_launch<T, MT, VL_LINEAR_STORE, true>(a, pdl, stream)
+                  : linear_launch<T, MT, VL_LINEAR_STORE, false>(a, pdl, stream);
     case VL_LINEAR_SWIGLU:
-      return norm ? linear_launch<T, MT, VL_LINEAR_SWIGLU, true>(a, stream)
-                  : linear_launch<T, MT, VL_LINEAR_SWIGLU, false>(a, stream);
+      return norm ? linear_launch<T, MT, VL_LINEAR_SWIGLU, true>(a, pdl, stream)
+                  : linear_launch<T, MT, VL_LINEAR_SWIGLU, false>(a, pdl, stream);
     default:
-      return norm ? linear_launch<T, MT, VL_LINEAR_RESIDUAL, true>(a, stream)
-                  : linear_launch<T, MT, VL_LINEAR_RESIDUAL, false>(a, stream);
+      return norm ? linear_launch<T, MT, VL_LINEAR_RESIDUAL, true>(a, pdl, stream)
+                  : linear_launch<T, MT, VL_LINEAR_RESIDUAL, false>(a, pdl, stream);
   }
 }
 
 template <typename T>
-cudaError_t linear_typed(const LinearArgs& a, cudaStream_t stream) {
-  if (a.rows <= 16) return linear_mt<T, 1>(a, stream);
-  if (a.rows <= 32) return linear_mt<T, 2>(a, stream);
-  return linear_mt<T, 4>(a, stream);
+cudaError_t linear_typed(const LinearArgs& a, bool pdl, cudaStream_t stream) {
+  if (a.rows <= 16) return linear_mt<T, 1>(a, pdl, stream);
+  if (a.rows <= 32) return linear_mt<T, 2>(a, pdl, stream);
+  return linear_mt<T, 4>(a, pdl, stream);
 }
 
 }  // namespace
 
-cudaError_t launch_decode_linear(const LinearArgs& a, int dtype, cudaStream_t stream) {
+cudaError_t launch_decode_linear(const LinearArgs& a, int dtype, bool pdl, cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;
-  if (dtype == kDtypeBF16) return linear_typed<__nv_bfloat16>(a, stream);
-  if (dtype == kDtypeF16) return linear_typed<__half>(a, stream);
+  if (dtype == kDtypeBF16) return linear_typed<__nv_bfloat16>(a, pdl, stream);
+  if (dtype == kDtypeF16) return linear_typed<__half>(a, pdl, stream);
   return cudaErrorInvalidValue;
 }
 

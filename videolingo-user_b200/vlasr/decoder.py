@@ -95,7 +95,9 @@ class TextDecoder:
         self.eos_ids = tuple(int(e) for e in eos_ids)
 
         def w(name):
-            return weights[name].to(device=self.device, dtype=dtype).contiguous()
+            t = weights[name].to(device=self.device, dtype=dtype).contiguous()
+            # the fused projections stage vectors with 16-byte copies
+            return t if t.data_ptr() % 16 == 0 else t.clone()
 
         self.embed = w("language_model.model.embed_tokens.weight")
         self.lm_head_t = w("language_model.lm_head.weight").t()
@@ -271,8 +273,27 @@ class TextDecoder:
             st["graph"].replay()
         return out[:max_new_tokens]
 
+    def replay_step(self, chunks: int, times: int = 1) -> None:
+        """Replay the captured decode step of `chunks` chunks `times` more
+        times, continuing from the state the last generate() left (for timing
+        the step alone).  The step counter and positions must stay inside the
+        id buffer and the KV caches."""
+        st = self._states.get(chunks)
+        if st is None or st["graph"] is None:
+            raise VlasrInputError(f"no captured decode step for {chunks} chunks: run generate()")
+        last = max(int(st["step"].item()), int(st["pos"].max().item())) + times
+        if last >= self.max_seq_len:
+            raise VlasrInputError(f"{times} more steps would pass max_seq_len {self.max_seq_len}")
+        for _ in range(times):
+            st["graph"].replay()
+
     def _step_fused(self, h: torch.Tensor, pos: torch.Tensor, start: torch.Tensor, k_cache,
                     v_cache, workspace: torch.Tensor):
+        """The five launches per layer run as programmatic dependents of the
+        launch before them (each streams weights, or cache rows of earlier
+        steps, while that one finishes): no launch of the step writes a
+        weight, the positions or slot starts, or a cache row before the
+        positions."""
         s = self.shape
         rows = h.shape[0]
         qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
@@ -282,21 +303,23 @@ class TextDecoder:
         for l, lw in enumerate(self.layer_w):
             if l == 0:      # the embedding rows have no partial sums: normalise them first
                 x = ops.add_rmsnorm(h, None, lw["ln1"], eps=s.eps)
-                qkv = ops.decode_linear(x, lw["qkv_t"].t())
+                qkv = ops.decode_linear(x, lw["qkv_t"].t(), pdl=True)
             else:
                 qkv = ops.decode_linear(h, lw["qkv_t"].t(), norm_weight=lw["ln1"], ssq_in=ssq_a,
-                                        eps=s.eps)
+                                        eps=s.eps, pdl=True)
             a = ops.decode_attention(qkv[:, :qw], k_cache[l], v_cache[l], pos, start,
                                      n_kv_heads=s.kv_heads, head_dim=s.head_dim,
                                      max_seq_len=self.max_seq_len, k=qkv[:, qw:qw + kw],
                                      v=qkv[:, qw + kw:], rotary_dim=s.head_dim,
-                                     rope_base=s.rope_base, workspace=workspace)
-            ops.decode_linear(a, lw["o_t"].t(), epilogue="residual", out=h, ssq_out=ssq_b)
+                                     rope_base=s.rope_base, workspace=workspace, pdl=True)
+            ops.decode_linear(a, lw["o_t"].t(), epilogue="residual", out=h, ssq_out=ssq_b,
+                              pdl=True)
             m = ops.decode_linear(h, lw["gu_t"].t(), norm_weight=lw["ln2"], ssq_in=ssq_b,
-                                  eps=s.eps, epilogue="swiglu")
-            ops.decode_linear(m, lw["down_t"].t(), epilogue="residual", out=h, ssq_out=ssq_a)
+                                  eps=s.eps, epilogue="swiglu", pdl=True)
+            ops.decode_linear(m, lw["down_t"].t(), epilogue="residual", out=h, ssq_out=ssq_a,
+                              pdl=True)
         logits = ops.decode_linear(h, self.lm_head_t.t(), norm_weight=self.norm_w, ssq_in=ssq_a,
-                                   eps=s.eps).float()
+                                   eps=s.eps, pdl=True).float()
         return logits.argmax(-1), logits
 
     def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,

@@ -338,7 +338,7 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      rope_base: float = 10000.0, scale: float = 0.0,
                      out: torch.Tensor | None = None,
                      workspace: torch.Tensor | None = None,
-                     status: torch.Tensor | None = None) -> torch.Tensor:
+                     status: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
     """One decode step of attention (vl_decode_attention).
 
     q [tokens, n_q_heads*head_dim] (or [tokens, n_q_heads, head_dim]; a row
@@ -349,7 +349,10 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     fused in.  max_seq_len bounds positions + 1 (a sequence's cache capacity):
     it sizes the split of the positions over CTAs, so pass the real bound.
     Without `workspace`, a zero-filled per-device workspace is used, which
-    serves calls in stream order on one stream."""
+    serves calls in stream order on one stream.  pdl=True launches it as a
+    programmatic dependent of the previous kernel on the stream
+    (VL_LAUNCH_PDL): that kernel must not write positions, seq_start or,
+    with k / v, the cache rows before the positions."""
     _same(q, k_cache, "k_cache")
     _same(q, v_cache, "v_cache")
     kvw = n_kv_heads * head_dim
@@ -392,7 +395,7 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         _ptr(seq_start), tokens, nq, n_kv_heads, head_dim, rotary_dim, float(rope_base),
         float(scale), qs, ks, cs, max_seq_len, num_slots, _ptr(out), os_, _dtype_code(q),
         _ptr(workspace), workspace.numel() * workspace.element_size(), _ptr(status),
-        _stream(q)), "vl_decode_attention")
+        LAUNCH_PDL if pdl else 0, _stream(q)), "vl_decode_attention")
     return out
 
 
@@ -401,13 +404,14 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
 # ---------------------------------------------------------------------------
 
 LINEAR_EPILOGUES = {"store": 0, "swiglu": 1, "residual": 2}
+LAUNCH_PDL = 1        # VL_LAUNCH_PDL
 LINEAR_MAX_ROWS = 64
 
 
 def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
                   out: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
                   ssq_in: torch.Tensor | None = None, eps: float = 1e-5,
-                  ssq_out: torch.Tensor | None = None) -> torch.Tensor:
+                  ssq_out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
     """y = x W^T for at most 64 token rows (vl_decode_linear).
 
     x [rows, k] (a row stride is allowed), w [n, k].  epilogue "store" -> out
@@ -415,7 +419,9 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
     out is the residual stream [rows, n], updated in place, and ssq_out
     (float32 [n/16, rows]) receives its per-16-column sums of squares.
     norm_weight + ssq_in (float32 [parts, rows], such partial sums) apply
-    the RMSNorm prologue to x."""
+    the RMSNorm prologue to x.  pdl=True launches it as a programmatic
+    dependent of the previous kernel on the stream (VL_LAUNCH_PDL): that
+    kernel must not write w or norm_weight."""
     if epilogue not in LINEAR_EPILOGUES:
         raise VlasrInputError(f"epilogue must be one of {sorted(LINEAR_EPILOGUES)}")
     _cuda(x, "x")
@@ -453,7 +459,7 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
     check(_lib.load().vl_decode_linear(
         _ptr(x), x.stride(0), _ptr(norm_weight), _ptr(ssq_in), parts, float(eps), _ptr(w), n, k,
         _ptr(out), out.stride(0), _ptr(ssq_out), rows, LINEAR_EPILOGUES[epilogue],
-        _dtype_code(x), _stream(x)), "vl_decode_linear")
+        _dtype_code(x), LAUNCH_PDL if pdl else 0, _stream(x)), "vl_decode_linear")
     return out
 
 
