@@ -210,12 +210,15 @@ def sum_over_ranks(x: float, world: int) -> float:
 def time_op(fn, iters: int, flush=None) -> float:
     """Mean device time (ms) of fn over `iters` launches, L2 flushed before each.
 
-    All iterations are enqueued before the one synchronisation, so the host
-    runs ahead of the GPU and each event pair brackets device time only (no
-    host launch gap)."""
+    All iterations are enqueued before the one synchronisation, behind a
+    device-side spin of about 0.5 ms per iteration (torch.cuda._sleep), so the
+    host is ahead of the GPU even for ops whose host wrapper takes longer than
+    the kernel: each event pair brackets device time only (no host launch
+    gap)."""
     import torch
     s = torch.cuda.current_stream()
     pairs = []
+    torch.cuda._sleep(1_000_000 * iters)      # ~0.5 ms per iteration at ~2 GHz
     for _ in range(iters):
         if flush is not None:
             flush()
@@ -346,6 +349,22 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
                                                head_dim=128, max_seq_len=4096, k=k, v=v,
                                                rotary_dim=128, out=out))
 
+    def decode_attention_engine():
+        # the engine's regime: 16 chunks at positions 400..415 after the
+        # 382-token prompt, 1024 slots per chunk, RoPE + append fused
+        slots = 1024
+        q, kv = rnd((16, 3072)), rnd((16 * slots, 2 * 512))
+        kc, vc = kv[:, :512], kv[:, 512:]
+        pos = (400 + torch.arange(16, device=dev, dtype=torch.int32)).contiguous()
+        start = torch.arange(16, device=dev, dtype=torch.int64) * slots
+        out = torch.empty(16, 2048, dtype=bf, device=dev)
+        nbytes = int(pos.sum()) * 2 * 512 * 2 + (2048 + 2 * 512) * 16 * 2 * 2
+        return ("16 chunks at positions 400..415 of 1024 slots, q|k|v rows [16,3072]", nbytes,
+                lambda: vlasr.decode_attention(q[:, :2048], kc, vc, pos, start, n_kv_heads=4,
+                                               head_dim=128, max_seq_len=slots,
+                                               k=q[:, 2048:2560], v=q[:, 2560:],
+                                               rotary_dim=128, out=out))
+
     def _decode_linear(kind):
         # one 16-row decode projection of the text decoder (hidden 2048, ffn 6144)
         rows, hid, ffn = 16, 2048, 6144
@@ -382,6 +401,7 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         ("decode_rope_kv_append", decode_rope_kv_append, 20, True),
         ("decode_attention", decode_attention, 20, False),
         ("decode_step_fused", decode_step_fused, 20, False),
+        ("decode_attention_engine", decode_attention_engine, 20, False),
         ("decode_linear_qkv_norm", lambda: _decode_linear("qkv_norm"), 20, False),
         ("decode_linear_gu_swiglu", lambda: _decode_linear("gu_swiglu"), 20, False),
         ("decode_linear_o_residual", lambda: _decode_linear("o_residual"), 20, False),
@@ -652,7 +672,7 @@ def run_linear_bench(args) -> None:
     y_qkv, y_gu, y_o = act(rows, 3072), act(rows, 6144), act(rows, 2048)
     y_gu_full = act(rows, 12288)
 
-    def graph_us(body):
+    def graph_us(body, count=layers):
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
@@ -671,7 +691,7 @@ def run_linear_bench(args) -> None:
         b.record()
         torch.cuda.synchronize()
         del graph
-        return round(a.elapsed_time(b) / reps / layers * 1e3, 2)
+        return round(a.elapsed_time(b) / reps / count * 1e3, 2)
 
     L = range(layers)
     fused = {
@@ -694,6 +714,35 @@ def run_linear_bench(args) -> None:
     mb = {"qkv": 3072 * 2048 * 2 / 1e6, "o": 2048 * 2048 * 2 / 1e6,
           "gu": 12288 * 2048 * 2 / 1e6, "down": 2048 * 6144 * 2 / 1e6}
     del w_qkv, w_o, w_gu, w_d
+    torch.cuda.empty_cache()
+    # RoPE + KV append + attention over 28 distinct caches (1024 slots per
+    # chunk), the chunks at positions 400..415 as after the 382-token prompt
+    slots = 1024
+    kc = [act(rows * slots, 512) for _ in L]
+    vc = [act(rows * slots, 512) for _ in L]
+    qkv = act(rows, 3072)
+    pos = (400 + torch.arange(rows, device=dev, dtype=torch.int32) % 16).contiguous()
+    start = torch.arange(rows, device=dev, dtype=torch.int64) * slots
+    ws = torch.zeros(ops.decode_attention_workspace_bytes(rows, 16, 4, 128, slots),
+                     dtype=torch.uint8, device=dev)
+    att = act(rows, 2048)
+    fused["attention"] = graph_us(lambda: [ops.decode_attention(
+        qkv[:, :2048], kc[i], vc[i], pos, start, n_kv_heads=4, head_dim=128, max_seq_len=slots,
+        k=qkv[:, 2048:2560], v=qkv[:, 2560:], rotary_dim=128, out=att, workspace=ws)
+        for i in L])
+    mb["attention"] = (int(pos.sum()) * 2 * 512 * 2 + 2 * qkv.numel() * 2) / 1e6
+    del kc, vc
+    torch.cuda.empty_cache()
+    # norm + lm_head (N = 59264) over 8 distinct matrices (1.9 GB)
+    heads = 8
+    w_lm = (torch.randn(heads, 59264, 2048, device=dev, generator=g) * 2048 ** -0.5).bfloat16()
+    logits = act(rows, 59264)
+    fused["lm_head_norm"] = graph_us(lambda: [ops.decode_linear(
+        h, w_lm[i], norm_weight=gam, ssq_in=ssq, out=logits) for i in range(heads)], heads)
+    cublas["lm_head"] = graph_us(lambda: [torch.mm(h, w_lm[i].t(), out=logits)
+                                          for i in range(heads)], heads)
+    mb["lm_head"] = 59264 * 2048 * 2 / 1e6
+    del w_lm
     torch.cuda.empty_cache()
 
     weights = {}

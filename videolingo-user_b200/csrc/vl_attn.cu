@@ -17,11 +17,15 @@
 // Here one CTA of 4 warps owns (token, kv head, split of the positions):
 // * the G = n_q_heads / n_kv_heads query heads that share the kv head are
 //   computed together, so each K and V row is read from HBM once;
-// * the split's K and V rows stream through a 2-stage shared-memory ring of
+// * the split's K and V rows stream through a shared-memory ring of
 //   64-position tiles (32 KB each) filled with cp.async (16 bytes per thread,
-//   L1 bypassed, rows past the end zero-filled): one tile loads while one is
-//   computed, and three CTAs share an SM; 16-byte chunks are XOR-swizzled by
-//   row so ldmatrix reads are free of bank conflicts;
+//   L1 bypassed, rows past the end zero-filled): 2 stages and three CTAs per
+//   SM when the grid fills the GPU, 3 or 4 stages when it does not; 16-byte
+//   chunks are XOR-swizzled by row so ldmatrix reads are free of bank
+//   conflicts;
+// * with programmatic dependent launch, the position, the first tiles and
+//   the rotation angles are fetched before waiting for the kernel that
+//   produces q and the new k / v rows;
 // * the products run on the tensor cores (mma.sync m16n8k16, fp32
 //   accumulate) with the positions as M and the query heads as N (GQA decode
 //   has too few queries for an M dimension): each warp takes 16 positions of
@@ -61,7 +65,14 @@ constexpr int kAttnWarps = kAttnThreads / 32;
 #define VL_ATTN_TARGET_CTAS 2048
 #endif
 constexpr int kTile = 64;                 // positions per pipeline tile (16 per warp)
-constexpr int kStages = VL_ATTN_STAGES;   // tiles in the ring
+#ifndef VL_ATTN_DEEP_RING
+#define VL_ATTN_DEEP_RING 1
+#endif
+// Tiles in the ring: VL_ATTN_STAGES (three CTAs per SM) for grids that fill
+// the GPU; with VL_ATTN_DEEP_RING, 3 (two per SM) for grids of at most two
+// CTAs per SM and 4 (one per SM) for at most one, so that more of a split's
+// tiles are in flight at once.
+constexpr int kStagesLarge = VL_ATTN_STAGES;
 constexpr int kMaxSplits = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -166,8 +177,8 @@ __device__ __forceinline__ int swz(int r, int c) {
   return r * HD + ((c ^ (r & 7)) << 3);
 }
 
-template <typename T, int HD, int G>
-__global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
+template <typename T, int HD, int G, int kStages>
+__global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : (kStages == 3 ? 2 : 1))
     decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a,
                             const __grid_constant__ InvFreq freq) {
   using S = Storage<T>;
@@ -239,6 +250,9 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
     if (st < ntiles) issue(st);
     cp_async_commit();
   }
+  // the rotation angles depend on the position only
+  for (int d = tid; d < half; d += kAttnThreads)
+    sm.cs[d] = rope_cos_sin(static_cast<double>(pos) * freq.v[d]);
   if (fresh) pdl_wait();
   pdl_release();
 
@@ -250,8 +264,6 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
     load_row_f32<T>(sm.vn, static_cast<const T*>(a.v) + t * a.kv_row_stride +
                                static_cast<int64_t>(h) * HD, HD, tid);
   }
-  for (int d = tid; d < half; d += kAttnThreads)
-    sm.cs[d] = rope_cos_sin(static_cast<double>(pos) * freq.v[d]);
   __syncthreads();
   if (rot > 0) {
     // RoPE on q and the fresh k, rounded to the storage type: the values the
@@ -524,14 +536,14 @@ __global__ void __launch_bounds__(kAttnThreads, kStages <= 2 ? 3 : 2)
   if (tid == 0) a.counters[pair] = 0;  // ready for the next call
 }
 
-template <typename T, int HD, int G>
-cudaError_t launch_typed(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream) {
+template <typename T, int HD, int G, int kStages>
+cudaError_t launch_staged(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream) {
   const InvFreq freq = make_inv_freq(a.rope_base, a.rotary_dim);
   constexpr size_t ring = static_cast<size_t>(kStages) * 2 * kTile * HD * sizeof(T);
   constexpr size_t partials = static_cast<size_t>(kAttnWarps) * G * HD * sizeof(float);
   constexpr size_t smem = attn_fixed_bytes<HD, G>() + (ring > partials ? ring : partials);
   static_assert(smem <= 227 * 1024, "decode attention shared memory");
-  auto kernel = decode_attention_kernel<T, HD, G>;
+  auto kernel = decode_attention_kernel<T, HD, G, kStages>;
   if (smem > 48 * 1024) {
     // once per device and instantiation, so that later launches (and CUDA
     // graph captures) make no further runtime calls
@@ -550,6 +562,15 @@ cudaError_t launch_typed(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream)
   const dim3 grid(static_cast<unsigned>(a.tokens), static_cast<unsigned>(a.n_kv_heads),
                   static_cast<unsigned>(a.max_splits));
   return launch_kernel(kernel, grid, dim3(kAttnThreads), smem, stream, pdl, a, freq);
+}
+
+template <typename T, int HD, int G>
+cudaError_t launch_typed(const DecodeAttnArgs& a, bool pdl, cudaStream_t stream) {
+  const int64_t ctas = a.tokens * a.n_kv_heads * a.max_splits;
+  const int64_t sms = sm_count();
+  if (VL_ATTN_DEEP_RING && ctas <= sms) return launch_staged<T, HD, G, 4>(a, pdl, stream);
+  if (VL_ATTN_DEEP_RING && ctas <= 2 * sms) return launch_staged<T, HD, G, 3>(a, pdl, stream);
+  return launch_staged<T, HD, G, kStagesLarge>(a, pdl, stream);
 }
 
 template <typename T>

@@ -46,6 +46,10 @@ from ._lib import VlasrInputError
 EOS_IDS = (59246, 59253, 59255)
 AUDIO_TOKEN_ID = 59260
 AUDIO_TOKENS_PER_CHUNK = 375
+# Decode steps of up to this many chunks run the fused layers (one 16-row
+# tile of vl_decode_linear per weight stream); larger batches run cuBLAS
+# GEMMs, which reuse each weight tile across more rows.
+FUSED_MAX_ROWS = 16
 
 
 @dataclass(frozen=True)
@@ -166,18 +170,19 @@ class TextDecoder:
         """One lockstep decode step for the active chunks: ids [chunks] (int64)
         are the current tokens, positions [chunks] (int32) their positions.
 
-        Up to 64 active chunks run the fused path: per layer vl_decode_linear
-        (RMSNorm prologue + q|k|v), vl_decode_attention, vl_decode_linear (o,
-        residual epilogue), vl_decode_linear (RMSNorm prologue + gate|up +
-        SwiGLU epilogue), vl_decode_linear (down, residual epilogue) - five
-        launches; more chunks run cuBLAS GEMMs between the standalone ops."""
+        Up to FUSED_MAX_ROWS active chunks run the fused path: per layer
+        vl_decode_linear (RMSNorm prologue + q|k|v), vl_decode_attention,
+        vl_decode_linear (o, residual epilogue), vl_decode_linear (RMSNorm
+        prologue + gate|up + SwiGLU epilogue), vl_decode_linear (down, residual
+        epilogue) - five launches; more chunks run cuBLAS GEMMs between the
+        standalone ops."""
         s = self.shape
         qw, kw = s.heads * s.head_dim, s.kv_heads * s.head_dim
         h = ops.embed_gather(ids.view(-1, 1), self.embed, row_map=active).view(-1, s.hidden)
         pos = positions[active.long()].contiguous()
         start = chunk_slots[active.long()].contiguous()
         rows = h.shape[0]
-        if self.fused and rows <= ops.LINEAR_MAX_ROWS:
+        if self.fused and rows <= FUSED_MAX_ROWS:
             return self._step_fused(h, pos, start, k_cache, v_cache, workspace)
         delta = None
         for l, lw in enumerate(self.layer_w):
@@ -316,11 +321,11 @@ class TextDecoder:
                               pdl=True)
             m = ops.decode_linear(h, lw["gu_t"].t(), norm_weight=lw["ln2"], ssq_in=ssq_b,
                                   eps=s.eps, epilogue="swiglu", pdl=True)
-            ops.decode_linear(m, lw["down_t"].t(), epilogue="residual", out=h, ssq_out=ssq_a,
-                              pdl=True)
-        logits = ops.decode_linear(h, self.lm_head_t.t(), norm_weight=self.norm_w, ssq_in=ssq_a,
-                                   eps=s.eps, pdl=True).float()
-        return logits.argmax(-1), logits
+            ops.decode_linear(m, lw["down_t"].t(), epilogue="residual", out=h,
+                              ssq_out=ssq_a if l + 1 < s.layers else None, pdl=True)
+        # final norm + lm_head: 3704 column tiles that would each re-read the
+        # rows; one norm launch and the cuBLAS GEMM stream the 243 MB faster
+        return self._argmax(h, None)
 
     def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,
                  forced_ids: list | None = None, graphs: bool = True) -> DecodeResult:
