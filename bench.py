@@ -134,25 +134,33 @@ class ClockSampler:
         except Exception:  # noqa: BLE001
             self.proc.kill()
         self._t.join(timeout=2)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
-                "samples": len(sm), "reasons": sorted(reasons)}
+        return summarize_clocks(self.lines)
+
+
+def summarize_clocks(lines) -> dict:
+    """nvidia-smi samples (FIELDS, csv, no header, no units) -> the `clocks`
+    object of the JSON line: median SM clock over the loaded samples (those
+    above half the highest; idle gaps excluded), the max clock, and every
+    throttle reason seen active."""
+    sm, smax, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in lines:
+        parts = [x.strip() for x in line.split(",")]
+        if len(parts) < 9:
+            continue
+        try:
+            sm.append(float(parts[1]))
+            smax.append(float(parts[2]))
+        except ValueError:
+            continue
+        for name, val in zip(names, parts[5:9]):
+            if val.lower() == "active":
+                reasons.add(name)
+    if not sm:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+    loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
+    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+            "samples": len(sm), "reasons": sorted(reasons)}
 
 
 # ---------------------------------------------------------------------------

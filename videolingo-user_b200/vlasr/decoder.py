@@ -27,10 +27,11 @@ Computes what the reference's cross-chunk batched decode computes
 
 Differences from the reference: every GEMM accumulates in fp32 (its default
 accumulates in fp16), q/k/v and gate/up are single GEMMs, attention keeps
-its scores on chip, the KV cache is not limited to 1024 positions, and the
-decode step (about 230 launches) is captured once in a CUDA graph and
-replayed, with the finished flags read every 8 steps instead of a host round
-trip and a re-compaction per step.
+its scores on chip, the KV cache is not limited to 1024 positions, up to
+16 chunks run each decode layer in five fused launches chained by
+programmatic dependent launch, and the decode step is captured once in a
+CUDA graph and replayed, with the finished flags read every 8 steps instead
+of a host round trip and a re-compaction per step.
 """
 
 from __future__ import annotations
