@@ -401,6 +401,36 @@ VL_EXPORT int vl_decode_linear(const void* x, int64_t x_row_stride, const void* 
                                int64_t y_row_stride, float* ssq_out, int64_t rows,
                                int epilogue, int dtype, int flags, void* stream);
 
+/*
+ * Decode-step tail: the greedy next token of each row with the EOS freeze,
+ * replacing the reference's argmax_mapped_kernel (native/asr/src/
+ * decoder.cu:573-621, launched at :1749) and, with finished = NULL, its
+ * argmax_rows_kernel (:755-782).
+ *
+ * Row r of logits ([rows][row_stride], vocab used; f32 / f16 / bf16) belongs
+ * to chunk c = row_chunk[r] (row_chunk NULL: c = r; c must be in
+ * [0, chunks)).  The id is the largest logit above -1e30 (NaN never wins);
+ * ties go to the smallest j mod 256, then the smallest j - the order of the
+ * reference's 256-thread reduction.  A row with no logit above -1e30 gives
+ * freeze_id (finished given) or 0.
+ * finished given ([chunks] bytes, 0/1): a finished chunk gives freeze_id
+ * without a scan and changes nothing else; otherwise, with out_ids, the id
+ * is stored at out_ids[(positions[c] - *prompt_length + 1) * out_stride + c]
+ * (an output row outside [0, out_rows) sets VL_STATUS_BAD_SLOT in *status
+ * instead), and an id in eos_ids[0..n_eos) marks the chunk finished.
+ * current_ids[c] = the id in every case.
+ * eos_ids is a HOST array (n_eos <= 8); prompt_length is a device scalar so
+ * a captured CUDA graph serves every prompt length.  Requires vocab % 8 == 0,
+ * vocab <= 2^24, row_stride % 8 == 0, 16-byte aligned logits.  No
+ * allocation, no synchronisation.
+ */
+VL_EXPORT int vl_argmax_eos(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                            const int32_t* row_chunk, int64_t chunks, uint8_t* finished,
+                            int64_t* current_ids, int64_t* out_ids, int64_t out_rows,
+                            int64_t out_stride, const int32_t* positions,
+                            const int64_t* prompt_length, const int64_t* eos_ids, int n_eos,
+                            int64_t freeze_id, int dtype, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

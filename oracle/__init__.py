@@ -56,11 +56,14 @@ def _load():
         lib.or_decode_attention.argtypes = [fp, c_void_p, c_void_p, fp, fp, POINTER(ctypes.c_int32),
                                             POINTER(c_int64), c_int64, c_int, c_int, c_int,
                                             c_int, c_double, c_float, c_int, fp]
+        lib.or_argmax_eos.argtypes = [fp, c_int64, c_int64, c_void_p, c_void_p,
+                                      POINTER(c_int64), c_void_p, c_void_p, c_int64, c_int64,
+                                      c_int64, POINTER(c_int64), c_int, c_int64]
         lib.or_mel_filterbank.argtypes = [POINTER(c_double)]
         lib.or_logmel_ref.argtypes = [fp, c_int64, fp]
         for name in ("or_round_array", "or_add_layernorm", "or_add_rmsnorm", "or_gelu",
                      "or_swiglu", "or_rope", "or_mel_filterbank", "or_logmel_ref",
-                     "or_decode_attention"):
+                     "or_decode_attention", "or_argmax_eos"):
             getattr(lib, name).restype = None
         _lib = lib
     return _lib
@@ -162,6 +165,35 @@ def decode_attention(q, k_cache, v_cache, positions, seq_start, *, k=None, v=Non
         pos.ctypes.data_as(POINTER(ctypes.c_int32)), st.ctypes.data_as(POINTER(c_int64)),
         tokens, nq, nkv, hd, rotary_dim, base, sc, DTYPE_CODES[dtype], _fp(out))
     return out, kc, vc
+
+
+def argmax_eos(logits, *, row_chunk=None, finished=None, current=None, out=None,
+               positions=None, prompt_length: int = 0, eos_ids=(), freeze_id: int = 59253):
+    """The reference's decode-step argmax (argmax_mapped_kernel; without
+    `finished`, argmax_rows_kernel).  logits [rows, vocab] (values of the
+    storage type); finished (uint8/bool [chunks]), current (int64 [chunks])
+    and out (int64 [out_rows, chunks]) are copied and returned updated:
+    (current, finished, out)."""
+    lg = _f32(logits)
+    rows, vocab = lg.shape
+    rc = None if row_chunk is None else np.ascontiguousarray(row_chunk, dtype=np.int32)
+    chunks = rows if rc is None else (int(rc.max()) + 1 if rows else 0)
+    if current is None:
+        cur = np.zeros(chunks, dtype=np.int64)
+    else:
+        cur = np.ascontiguousarray(current, dtype=np.int64).copy()
+    fin = None if finished is None else np.ascontiguousarray(finished, dtype=np.uint8).copy()
+    oo = None if out is None else np.ascontiguousarray(out, dtype=np.int64).copy()
+    pos = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
+    eos = np.ascontiguousarray(list(eos_ids) or [0], dtype=np.int64)
+    _load().or_argmax_eos(
+        _fp(lg), rows, vocab, None if rc is None else rc.ctypes.data_as(c_void_p),
+        None if fin is None else fin.ctypes.data_as(c_void_p), cur.ctypes.data_as(POINTER(c_int64)),
+        None if oo is None else oo.ctypes.data_as(c_void_p),
+        None if pos is None else pos.ctypes.data_as(c_void_p), int(prompt_length),
+        0 if oo is None else oo.shape[0], 0 if oo is None else oo.shape[1],
+        eos.ctypes.data_as(POINTER(c_int64)), len(eos_ids), int(freeze_id))
+    return cur, fin, oo
 
 
 def mel_filterbank_f64() -> np.ndarray:

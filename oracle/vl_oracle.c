@@ -340,3 +340,66 @@ void or_decode_attention(float* q, float* k_new, const float* v_new, float* k_ca
     free(scores);
   }
 }
+
+/*
+ * Greedy next token with the EOS freeze: argmax_mapped_kernel
+ * (decoder.cu:573-621); with finished == NULL, argmax_rows_kernel
+ * (decoder.cu:755-782).  Logits are float32 holding storage values.
+ *
+ * Per row r (chunk c = row_chunk ? row_chunk[r] : r), as the reference's
+ * 256-thread block computes it: thread t scans j = t, t+256, ... from -1e30
+ * and keeps the first strictly greater value; thread 0 then scans the
+ * threads in order from -1e30 and keeps the first strictly greater one.  A
+ * row with no value above -1e30 yields freeze_id when finished is given
+ * (the mapped kernel's initial winner) and 0 otherwise.
+ * With finished: a finished chunk yields freeze_id and nothing else
+ * changes; otherwise out_ids[(positions[c] - prompt_length + 1) *
+ * out_stride + c] = id (when out_ids and the row is in [0, out_rows)) and
+ * the chunk becomes finished when id is one of eos[0..n_eos).  current_ids[c]
+ * = id in every case.
+ */
+void or_argmax_eos(const float* logits, int64_t rows, int64_t vocab, const int32_t* row_chunk,
+                   uint8_t* finished, int64_t* current_ids, int64_t* out_ids,
+                   const int32_t* positions, int64_t prompt_length, int64_t out_rows,
+                   int64_t out_stride, const int64_t* eos, int n_eos, int64_t freeze_id) {
+  enum { kThreads = 256 };
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t c = row_chunk ? row_chunk[r] : r;
+    if (finished && finished[c]) {
+      current_ids[c] = freeze_id;
+      continue;
+    }
+    const float* row = logits + r * vocab;
+    float local_best[kThreads];
+    int64_t local_index[kThreads];
+    for (int t = 0; t < kThreads; ++t) {
+      float best = -1e30f;
+      int64_t index = 0;
+      for (int64_t j = t; j < vocab; j += kThreads) {
+        if (row[j] > best) {
+          best = row[j];
+          index = j;
+        }
+      }
+      local_best[t] = best;
+      local_index[t] = index;
+    }
+    float overall = -1e30f;
+    int64_t winner = finished ? freeze_id : 0;
+    for (int t = 0; t < kThreads; ++t) {
+      if (local_best[t] > overall) {
+        overall = local_best[t];
+        winner = local_index[t];
+      }
+    }
+    if (finished) {
+      if (out_ids) {
+        const int64_t orow = (int64_t)positions[c] - prompt_length + 1;
+        if (orow >= 0 && orow < out_rows) out_ids[orow * out_stride + c] = winner;
+      }
+      for (int e = 0; e < n_eos; ++e)
+        if (winner == eos[e]) finished[c] = 1;
+    }
+    current_ids[c] = winner;
+  }
+}

@@ -31,7 +31,7 @@ def test_header_declares_the_expected_ops():
     for name in ("vl_logmel", "vl_add_layernorm", "vl_add_rmsnorm", "vl_gelu_erf", "vl_swiglu",
                  "vl_rope_inplace", "vl_embed_gather", "vl_kv_append", "vl_rope_kv_append",
                  "vl_decode_attention", "vl_decode_attention_workspace_bytes",
-                 "vl_decode_linear",
+                 "vl_decode_linear", "vl_argmax_eos",
                  "vl_last_error", "vl_logmel_workspace_bytes"):
         assert name in syms
 
@@ -190,6 +190,30 @@ def test_decode_linear_rejects(lib):
     assert call(y=FAKE) == 2 and "overlaps" in _err(lib)
     assert call(flags=4) == 2 and "flags" in _err(lib)
     assert call(g=FAKE * 3 + 4, ssq=FAKE * 4, parts=128) == 2 and "norm_weight" in _err(lib)
+
+
+def test_argmax_eos_rejects(lib):
+    import ctypes
+    eos = (ctypes.c_int64 * 3)(59246, 59253, 59255)
+
+    def call(lg=FAKE, rows=16, vocab=59264, rs=59264, rc=None, chunks=16, fin=FAKE * 2,
+             cur=FAKE * 3, out=None, out_rows=0, out_stride=0, pos=None, plen=None, n_eos=3,
+             dtype=2):
+        return lib.vl_argmax_eos(lg, rows, vocab, rs, rc, chunks, fin, cur, out, out_rows,
+                                 out_stride, pos, plen, eos, n_eos, 59253, dtype, None, None)
+
+    assert call(lg=None) == 2 and "null" in _err(lib)
+    assert call(dtype=5) == 2 and "dtype" in _err(lib)
+    assert call(chunks=8) == 2 and "rows" in _err(lib)
+    assert call(vocab=59260, rs=59260) == 2 and "vocab" in _err(lib)
+    assert call(vocab=1 << 25, rs=1 << 25) == 2 and "vocab" in _err(lib)
+    assert call(rs=59268) == 2 and "stride" in _err(lib)
+    assert call(lg=FAKE + 8) == 2 and "aligned" in _err(lib)
+    assert call(n_eos=9) == 2 and "n_eos" in _err(lib)
+    assert call(out=FAKE * 4, out_rows=1024, out_stride=16) == 2 and "positions" in _err(lib)
+    assert call(out=FAKE * 4, out_rows=1024, out_stride=8, pos=FAKE * 5, plen=FAKE * 6) == 2
+    assert "out_stride" in _err(lib)
+    assert call(rows=0, chunks=0) == 0
 
 
 def test_error_is_thread_local(lib):

@@ -530,4 +530,53 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
                      op);
 }
 
+int vl_argmax_eos(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                  const int32_t* row_chunk, int64_t chunks, uint8_t* finished,
+                  int64_t* current_ids, int64_t* out_ids, int64_t out_rows, int64_t out_stride,
+                  const int32_t* positions, const int64_t* prompt_length,
+                  const int64_t* eos_ids, int n_eos, int64_t freeze_id, int dtype,
+                  int32_t* status, void* stream) {
+  const char* op = "vl_argmax_eos";
+  if (logits == nullptr || current_ids == nullptr)
+    return fail(VL_ERR_INVALID, "%s: null pointer", op);
+  if (dtype != VL_F32 && dtype != VL_F16 && dtype != VL_BF16)
+    return fail(VL_ERR_INVALID, "%s: unsupported dtype %d", op, dtype);
+  if (rows < 0 || rows > 0x7fffffff || chunks < 0 || (row_chunk == nullptr && chunks < rows))
+    return fail(VL_ERR_INVALID, "%s: bad rows=%lld chunks=%lld", op,
+                static_cast<long long>(rows), static_cast<long long>(chunks));
+  if (vocab <= 0 || vocab % 8 != 0 || vocab > (int64_t(1) << 24))
+    return fail(VL_ERR_INVALID, "%s: vocab must be a positive multiple of 8, at most 2^24", op);
+  if (row_stride < vocab || row_stride % 8 != 0)
+    return fail(VL_ERR_INVALID, "%s: bad row stride", op);
+  if (!vl::aligned16(logits))
+    return fail(VL_ERR_INVALID, "%s: logits must be 16-byte aligned", op);
+  if (n_eos < 0 || n_eos > 8 || (n_eos > 0 && eos_ids == nullptr))
+    return fail(VL_ERR_INVALID, "%s: n_eos must be in [0, 8] with eos_ids given", op);
+  if (out_ids != nullptr) {
+    if (finished == nullptr || positions == nullptr || prompt_length == nullptr)
+      return fail(VL_ERR_INVALID, "%s: out_ids needs finished, positions and prompt_length", op);
+    if (out_rows <= 0 || out_stride < chunks)
+      return fail(VL_ERR_INVALID, "%s: bad out_rows / out_stride", op);
+  }
+  vl::ArgmaxArgs a{};
+  a.logits = logits;
+  a.rows = rows;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.row_chunk = row_chunk;
+  a.chunks = chunks;
+  a.finished = finished;
+  a.current_ids = current_ids;
+  a.out_ids = out_ids;
+  a.out_rows = out_rows;
+  a.out_stride = out_stride;
+  a.positions = positions;
+  a.prompt_length = prompt_length;
+  for (int e = 0; e < n_eos; ++e) a.eos[e] = eos_ids[e];
+  a.n_eos = n_eos;
+  a.freeze_id = freeze_id;
+  a.status = status;
+  return exec_status(vl::launch_argmax_eos(a, dtype, static_cast<cudaStream_t>(stream)), op);
+}
+
 }  // extern "C"

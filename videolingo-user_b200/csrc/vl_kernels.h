@@ -118,6 +118,28 @@ struct LinearArgs {
 cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, bool pdl,
                                  cudaStream_t stream);
 
+// Decode-step tail: argmax with the EOS freeze (vl_argmax.cu).
+struct ArgmaxArgs {
+  const void* logits;            // [rows][row_stride], vocab used
+  int64_t rows;
+  int64_t vocab;
+  int64_t row_stride;
+  const int32_t* row_chunk;      // [rows] chunk of each row, or nullptr (row = chunk)
+  int64_t chunks;
+  uint8_t* finished;             // [chunks] or nullptr (plain argmax)
+  int64_t* current_ids;          // [chunks]
+  int64_t* out_ids;              // [out_rows][out_stride] or nullptr
+  int64_t out_rows;
+  int64_t out_stride;
+  const int32_t* positions;      // [chunks]
+  const int64_t* prompt_length;  // device scalar
+  int64_t eos[8];
+  int n_eos;
+  int64_t freeze_id;
+  int32_t* status;
+};
+cudaError_t launch_argmax_eos(const ArgmaxArgs& args, int dtype, cudaStream_t stream);
+
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream);

@@ -133,11 +133,16 @@ class TextDecoder:
         m = ops.swiglu(gu[:, :s.ffn], gu[:, s.ffn:])
         return m @ lw["down_t"]
 
+    def _logits(self, h: torch.Tensor, delta: torch.Tensor | None) -> torch.Tensor:
+        """Final RMSNorm of h + delta and the lm_head: [rows, vocab] in the
+        compute dtype."""
+        y = ops.add_rmsnorm(h, delta, self.norm_w, eps=self.shape.eps)
+        return y @ self.lm_head_t
+
     def _argmax(self, h: torch.Tensor, delta: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        s = self.shape
-        y = ops.add_rmsnorm(h, delta, self.norm_w, eps=s.eps)
-        logits = (y @ self.lm_head_t).float()
-        return logits.argmax(-1), logits
+        """(ids, float32 logits); the ids in the reference's tie order."""
+        logits = self._logits(h, delta)
+        return ops.argmax_eos(logits), logits.float()
 
     def prefill(self, audio: torch.Tensor, prompt: torch.Tensor, k_cache, v_cache,
                 chunk_slots: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -168,8 +173,18 @@ class TextDecoder:
 
     def step(self, ids: torch.Tensor, active: torch.Tensor, positions: torch.Tensor,
              k_cache, v_cache, chunk_slots: torch.Tensor, workspace: torch.Tensor):
+        """One lockstep decode step -> (next ids, float32 logits) of the
+        active rows (see step_logits)."""
+        logits = self.step_logits(ids, active, positions, k_cache, v_cache, chunk_slots,
+                                  workspace)
+        return ops.argmax_eos(logits), logits.float()
+
+    def step_logits(self, ids: torch.Tensor, active: torch.Tensor, positions: torch.Tensor,
+                    k_cache, v_cache, chunk_slots: torch.Tensor,
+                    workspace: torch.Tensor) -> torch.Tensor:
         """One lockstep decode step for the active chunks: ids [chunks] (int64)
-        are the current tokens, positions [chunks] (int32) their positions.
+        are the current tokens, positions [chunks] (int32) their positions;
+        returns the logits of the active rows in the compute dtype.
 
         Up to FUSED_MAX_ROWS active chunks run the fused path: per layer
         vl_decode_linear (RMSNorm prologue + q|k|v), vl_decode_attention,
@@ -195,7 +210,7 @@ class TextDecoder:
                                      v=qkv[:, qw + kw:], rotary_dim=s.head_dim,
                                      rope_base=s.rope_base, workspace=workspace)
             delta = self._mlp(lw, h, a @ lw["o_t"])
-        return self._argmax(h, delta)
+        return self._logits(h, delta)
 
     def _state(self, chunks: int) -> dict:
         """Per chunk count: KV caches, decode workspace and the step buffers a
@@ -220,26 +235,25 @@ class TextDecoder:
             "cur": torch.zeros(chunks, dtype=torch.int64, device=dev),
             "fin": torch.zeros(chunks, dtype=torch.bool, device=dev),
             "pos": torch.zeros(chunks, dtype=torch.int32, device=dev),
-            "step": torch.ones((), dtype=torch.int64, device=dev),
+            "prompt_len": torch.zeros((), dtype=torch.int64, device=dev),
             "rows": torch.arange(chunks, device=dev, dtype=torch.int32),
-            "lanes": torch.arange(chunks, device=dev, dtype=torch.int64),
-            "frozen": torch.full((chunks,), self.eos_ids[1], dtype=torch.int64, device=dev),
             "graph": None,
         }
         self._states[chunks] = st
         return st
 
     def _decode_body(self, st: dict) -> None:
-        """One lockstep step over every chunk of `st` (device state only)."""
-        chunks = st["cur"].numel()
-        nxt, _ = self.step(st["cur"], st["rows"], st["pos"], st["k_cache"], st["v_cache"],
-                           st["chunk_slots"], st["ws"])
-        nxt = torch.where(st["fin"], st["frozen"], nxt)
-        st["out"].view(-1).index_copy_(0, st["step"] * chunks + st["lanes"], nxt)
-        st["fin"].logical_or_(torch.isin(nxt, self.eos))
-        st["cur"].copy_(nxt)
+        """One lockstep step over every chunk of `st` (device state only):
+        the layers, then one vl_argmax_eos launch for the reference's tail
+        (argmax_mapped_kernel: freeze finished chunks, store the id at row
+        position - prompt length + 1, finish on EOS, update the current ids)
+        and the position advance."""
+        logits = self.step_logits(st["cur"], st["rows"], st["pos"], st["k_cache"],
+                                  st["v_cache"], st["chunk_slots"], st["ws"])
+        ops.argmax_eos(logits, current=st["cur"], finished=st["fin"], out=st["out"],
+                       positions=st["pos"], prompt_length=st["prompt_len"],
+                       eos_ids=self.eos_ids, freeze_id=self.eos_ids[1])
         st["pos"].add_(1)
-        st["step"].add_(1)
 
     def _generate_graphed(self, st: dict, first: torch.Tensor, L: int,
                           max_new_tokens: int) -> torch.Tensor:
@@ -247,17 +261,17 @@ class TextDecoder:
         chunk count; later calls replay it).
 
         Every chunk stays in the batch; a finished chunk emits 59253 (the
-        reference's argmax_mapped_kernel freeze) and its rows are ignored when
-        the ids are collected.  Without a graph yet, step 1 runs eagerly (it
-        also warms the libraries up) before the capture; the finished flags
-        are read every 8 steps."""
+        reference's argmax_mapped_kernel freeze) into the current ids and
+        stores nothing.  Without a graph yet, step 1 runs eagerly (it also
+        warms the libraries up) before the capture; the finished flags are
+        read every 8 steps."""
         out = st["out"]
         out.fill_(-1)
         out[0] = first
         st["cur"].copy_(first)
         torch.isin(first, self.eos, out=st["fin"])
         st["pos"].fill_(L)
-        st["step"].fill_(1)
+        st["prompt_len"].fill_(L)
         if max_new_tokens <= 1:
             return out[:max_new_tokens]
         dev = self.device
@@ -282,12 +296,12 @@ class TextDecoder:
     def replay_step(self, chunks: int, times: int = 1) -> None:
         """Replay the captured decode step of `chunks` chunks `times` more
         times, continuing from the state the last generate() left (for timing
-        the step alone).  The step counter and positions must stay inside the
-        id buffer and the KV caches."""
+        the step alone).  The positions (and with them the id rows) must stay
+        inside the KV caches."""
         st = self._states.get(chunks)
         if st is None or st["graph"] is None:
             raise VlasrInputError(f"no captured decode step for {chunks} chunks: run generate()")
-        last = max(int(st["step"].item()), int(st["pos"].max().item())) + times
+        last = int(st["pos"].max().item()) + times
         if last >= self.max_seq_len:
             raise VlasrInputError(f"{times} more steps would pass max_seq_len {self.max_seq_len}")
         for _ in range(times):
@@ -326,7 +340,7 @@ class TextDecoder:
                               ssq_out=ssq_a if l + 1 < s.layers else None, pdl=True)
         # final norm + lm_head: 3704 column tiles that would each re-read the
         # rows; one norm launch and the cuBLAS GEMM stream the 243 MB faster
-        return self._argmax(h, None)
+        return self._logits(h, None)
 
     def generate(self, audio: torch.Tensor, prompt_ids, max_new_tokens: int = 256,
                  forced_ids: list | None = None, graphs: bool = True) -> DecodeResult:

@@ -24,6 +24,8 @@ logmel                 compute_mel_batched (mel_frontend.cu:209-291)
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -461,6 +463,69 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
         _ptr(out), out.stride(0), _ptr(ssq_out), rows, LINEAR_EPILOGUES[epilogue],
         _dtype_code(x), LAUNCH_PDL if pdl else 0, _stream(x)), "vl_decode_linear")
     return out
+
+
+# ---------------------------------------------------------------------------
+# Decode-step tail
+# ---------------------------------------------------------------------------
+
+def argmax_eos(logits: torch.Tensor, *, current: torch.Tensor | None = None,
+               finished: torch.Tensor | None = None, row_chunk: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, positions: torch.Tensor | None = None,
+               prompt_length: torch.Tensor | None = None, eos_ids=(), freeze_id: int = 59253,
+               status: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy next token per row with the reference's tie order and EOS
+    freeze (vl_argmax_eos).  logits [rows, vocab] (a row stride is allowed).
+
+    Without `finished`: plain argmax per row (current [rows] is returned).
+    With finished (bool/uint8 [chunks]), current (int64 [chunks]) and
+    optionally row_chunk (int32 [rows]), out (int64 [out_rows, chunks]),
+    positions (int32 [chunks]) and prompt_length (int64 device scalar): the
+    whole decode-step tail - finished chunks give freeze_id, others store
+    their id at out[positions - prompt_length + 1] and finish on an EOS id.
+    Returns `current`."""
+    _cuda(logits, "logits")
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise VlasrInputError("logits must be a 2-D tensor with contiguous rows")
+    rows, vocab = logits.shape
+    if row_chunk is not None:
+        _contig(row_chunk, "row_chunk")
+        if row_chunk.dtype != torch.int32 or row_chunk.numel() != rows:
+            raise VlasrInputError("row_chunk must be int32 with one entry per row")
+    if current is None:
+        if finished is not None or row_chunk is not None:
+            raise VlasrInputError("pass `current` (int64 [chunks]) with finished / row_chunk")
+        current = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    _contig(current, "current")
+    if current.dtype != torch.int64 or current.dim() != 1:
+        raise VlasrInputError("current must be int64 [chunks]")
+    chunks = current.numel()
+    if finished is not None:
+        _contig(finished, "finished")
+        if finished.dtype not in (torch.bool, torch.uint8) or finished.numel() != chunks:
+            raise VlasrInputError("finished must be bool/uint8 [chunks]")
+    out_rows = out_stride = 0
+    if out is not None:
+        _contig(out, "out")
+        if out.dtype != torch.int64 or out.dim() != 2 or out.shape[1] != chunks:
+            raise VlasrInputError("out must be int64 [out_rows, chunks]")
+        out_rows, out_stride = out.shape
+        for name, t, dt in (("positions", positions, torch.int32),
+                            ("prompt_length", prompt_length, torch.int64)):
+            if t is None:
+                raise VlasrInputError(f"out needs {name}")
+            _contig(t, name)
+            if t.dtype != dt:
+                raise VlasrInputError(f"{name} must be {dt}")
+        if positions.numel() != chunks or prompt_length.numel() != 1:
+            raise VlasrInputError("positions must be [chunks] and prompt_length a scalar")
+    eos = (ctypes.c_int64 * max(len(eos_ids), 1))(*[int(e) for e in eos_ids])
+    check(_lib.load().vl_argmax_eos(
+        _ptr(logits), rows, vocab, logits.stride(0), _ptr(row_chunk), chunks, _ptr(finished),
+        _ptr(current), _ptr(out), out_rows, out_stride, _ptr(positions), _ptr(prompt_length),
+        eos, len(eos_ids), int(freeze_id), _dtype_code(logits), _ptr(status),
+        _stream(logits)), "vl_argmax_eos")
+    return current
 
 
 # ---------------------------------------------------------------------------
