@@ -27,10 +27,19 @@
  *     returns the message of the last failure on the calling thread.
  *   - Invalid arguments are detected on the host before any CUDA call, so a
  *     rejected call has no side effects and needs no GPU.
- *   - Buffers are caller-owned DEVICE pointers; ops never allocate, never
- *     synchronise and run on the caller's stream (`stream` is a cudaStream_t
- *     passed as void*; NULL = the legacy default stream).
- *   - Ops are stateless and thread-safe; launches on one stream are ordered.
+ *   - Buffers are caller-owned DEVICE pointers; ops never allocate device
+ *     memory and run on the caller's stream (`stream` is a cudaStream_t
+ *     passed as void*; NULL = the legacy default stream).  After an op's
+ *     first call on a device they never synchronise either.  The first call
+ *     does per-device set-up, cached for the life of the process: kernel
+ *     attributes and occupancy queries for every op, and for vl_gelu_erf
+ *     (f16/bf16) a one-time table build that launches one kernel on a
+ *     private stream and waits for it.  vl_init() does all of it up front.
+ *   - Apart from that per-device set-up (built once, read-only afterwards),
+ *     ops keep no state between calls and are thread-safe; launches on one
+ *     stream are ordered.  The exceptions that keep device state across
+ *     calls (vl_decode_attention's split counters in the caller's
+ *     workspace, vl_logmel_noalloc's fixed scratch array) say so below.
  *   - Float ops compute in fp32 and round once to the storage type (RNE);
  *     the rounding points are those of the reference kernels (documented per
  *     op below).  Index ops (gather, KV append) are bit-exact copies.
@@ -86,6 +95,30 @@ VL_EXPORT const char* vl_last_error(void);
 
 /* Number of CUDA devices visible to the library (0 on a host without GPU). */
 VL_EXPORT int vl_device_count(void);
+
+/*
+ * Once-per-device set-up, ahead of the first op call on `device` (the
+ * caller's current device is restored on return).  Optional: each op does
+ * its own part of it on its first call on a device, which is what this call
+ * moves out of the hot path and out of any stream capture.  What it does:
+ *   - builds the GELU lookup tables that vl_gelu_erf uses for f16/bf16
+ *     inputs of 1M elements or more: creates a private stream, launches one
+ *     kernel on it, synchronises that stream and destroys it (the only op
+ *     set-up that launches work or waits); the tables live in a fixed
+ *     256 KB array inside the library, so nothing is allocated;
+ *   - raises the shared-memory limit of the log-mel kernel
+ *     (cudaFuncSetAttribute) and looks up the address of
+ *     vl_logmel_noalloc's fixed scratch array (cudaGetSymbolAddress).
+ * The other ops' first-call set-up only sets kernel attributes and queries
+ * occupancy (host calls that neither launch, allocate nor wait).
+ * Without vl_init, the first vl_gelu_erf call on a device made while its
+ * stream is being captured cannot build the tables; that call and the graph
+ * captured with it evaluate erff directly, with bit-identical results but
+ * at lower speed, and the tables are built by the first later call that is
+ * not captured.  Returns VL_ERR_INVALID for a bad device index or when
+ * called during a capture of the legacy stream.
+ */
+VL_EXPORT int vl_init(int device);
 
 /* ------------------------------------------------------------------------ */
 /* Log-mel frontend                                                          */
@@ -420,7 +453,11 @@ VL_EXPORT int vl_decode_linear(const void* x, int64_t x_row_stride, const void* 
  * instead), and an id in eos_ids[0..n_eos) marks the chunk finished.
  * current_ids[c] = the id in every case.
  * eos_ids is a HOST array (n_eos <= 8); prompt_length is a device scalar so
- * a captured CUDA graph serves every prompt length.  Requires vocab % 8 == 0,
+ * a captured CUDA graph serves every prompt length.  With finished given,
+ * row_chunk entries must be distinct: two rows of one chunk would both write
+ * finished[c], current_ids[c] and the chunk's out_ids slot with no order
+ * between them, and which id lands there is unspecified (row_chunk lives in
+ * device memory, so this is not checked).  Requires vocab % 8 == 0,
  * vocab <= 2^24, row_stride % 8 == 0, 16-byte aligned logits.  No
  * allocation, no synchronisation.
  */

@@ -22,7 +22,11 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
 REF_LIB = REF_DIR / "libvlref.so"
-REF_SRC = Path(os.environ.get("VL_REFERENCE_SRC", "/root/reference/native/asr/src"))
+# The reference checkout: $VL_REFERENCE_SRC, else a `reference` directory
+# beside this repository (its native/asr/src).  Absent on hosts that only run
+# the prebuilt libraries.
+REF_SRC = Path(os.environ.get("VL_REFERENCE_SRC")
+               or HERE.parent.parent / "reference" / "native" / "asr" / "src")
 
 
 def build_oracle(force: bool = False) -> Path:

@@ -53,6 +53,14 @@ def test_version_and_device_count(lib):
     assert lib.vl_device_count() >= 0
 
 
+def test_init_rejects_a_device_that_does_not_exist(lib):
+    # no GPU here: every index is out of range; on a GPU box, count is the bound
+    n = lib.vl_device_count()
+    assert lib.vl_init(n) == _lib.VL_ERR_INVALID
+    assert lib.vl_init(-1) == _lib.VL_ERR_INVALID
+    assert "vl_init" in lib.vl_last_error().decode()
+
+
 def test_logmel_workspace_bytes(lib):
     assert lib.vl_logmel_workspace_bytes(0) == 0
     ws1 = lib.vl_logmel_workspace_bytes(1)

@@ -88,7 +88,8 @@ def test_teacher_forced_steps_match_reference(decoders, audio16, reference_ids, 
           f"disagreements (step, chunk, margin): {ties}")
     near = NEAR_TIE if dt == torch.float16 else 4 * NEAR_TIE
     assert all(m < near for _, _, m in ties), ties
-    assert same >= 0.9 * total
+    # measured: every teacher-forced step agrees; allow one near tie in 32
+    assert total - same <= max(1, total // 32), (same, total)
 
 
 def test_free_running_first_tokens(decoders, audio16, reference_ids):

@@ -425,6 +425,14 @@ cudaError_t swiglu_typed(const void* gate, const void* up, void* out, int64_t ro
 
 }  // namespace
 
+cudaError_t prepare_gelu() {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t err = cudaStreamIsCapturing(nullptr, &cap);
+  if (err != cudaSuccess) return err;
+  if (cap != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
+  return gelu_table(nullptr) != nullptr ? cudaSuccess : cudaErrorUnknown;
+}
+
 cudaError_t launch_gelu(const void* in, const void* bias, void* out, int64_t rows, int64_t cols,
                         int dtype, cudaStream_t stream) {
   if (rows == 0 || cols == 0) return cudaSuccess;

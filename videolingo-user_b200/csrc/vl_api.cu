@@ -110,6 +110,30 @@ int vl_device_count(void) {
   return n;
 }
 
+int vl_init(int device) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    (void)cudaGetLastError();
+    count = 0;
+  }
+  if (device < 0 || device >= count)
+    return fail(VL_ERR_INVALID, "vl_init: device %d not in [0, %d)", device, count);
+  int prev = 0;
+  cudaError_t err = cudaGetDevice(&prev);
+  if (err == cudaSuccess) err = cudaSetDevice(device);
+  if (err != cudaSuccess) return exec_status(err, "vl_init");
+  (void)vl::sm_count();
+  err = vl::prepare_gelu();
+  if (err == cudaErrorStreamCaptureUnsupported) {
+    (void)cudaSetDevice(prev);
+    return fail(VL_ERR_INVALID, "vl_init: called while the legacy stream is being captured");
+  }
+  if (err == cudaSuccess) err = vl::prepare_logmel();
+  const cudaError_t restore = cudaSetDevice(prev);
+  if (err == cudaSuccess) err = restore;
+  return exec_status(err, "vl_init");
+}
+
 size_t vl_logmel_workspace_bytes(int64_t chunks) {
   if (chunks <= 0 || chunks > kMaxMelChunks) return 0;
   return vl::logmel_workspace_bytes(chunks);

@@ -140,6 +140,12 @@ struct ArgmaxArgs {
 };
 cudaError_t launch_argmax_eos(const ArgmaxArgs& args, int dtype, cudaStream_t stream);
 
+// Once-per-device set-up done ahead of the first op call (vl_init): the
+// GELU tables (a private stream, one kernel, one stream synchronise) and the
+// log-mel kernel's shared-memory limit and scratch address.
+cudaError_t prepare_gelu();
+cudaError_t prepare_logmel();
+
 size_t logmel_workspace_bytes(int64_t chunks);
 cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* tile_max,
                           cudaStream_t stream);

@@ -352,22 +352,29 @@ static __device__ __align__(256) float g_noalloc_tile_max[VL_LOGMEL_NOALLOC_MAX_
 }  // namespace
 
 // Device address of g_noalloc_tile_max on the current device, looked up on
-// the first call per device (that device current) and cached.
+// the first call per device (that device current) and cached.  Later calls
+// read the cached address with one acquire load; only the first lookup on a
+// device takes the lock.
 cudaError_t noalloc_tile_max(float** ptr) {
   static std::mutex mu;
-  static float* addr[64] = {};
+  static std::atomic<float*> addr[64];
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_noalloc_tile_max);
-    if (err != cudaSuccess) return err;
-    addr[dev] = static_cast<float*>(p);
+  float* cached = addr[dev].load(std::memory_order_acquire);
+  if (cached == nullptr) {
+    std::lock_guard<std::mutex> lock(mu);
+    cached = addr[dev].load(std::memory_order_relaxed);
+    if (cached == nullptr) {
+      void* p = nullptr;
+      err = cudaGetSymbolAddress(&p, g_noalloc_tile_max);
+      if (err != cudaSuccess) return err;
+      cached = static_cast<float*>(p);
+      addr[dev].store(cached, std::memory_order_release);
+    }
   }
-  *ptr = addr[dev];
+  *ptr = cached;
   return cudaSuccess;
 }
 
@@ -401,6 +408,13 @@ cudaError_t launch_logmel(const float* pcm, int64_t chunks, float* out, float* t
 }  // namespace vl
 
 namespace vl {
+
+cudaError_t prepare_logmel() {
+  float* tile_max = nullptr;
+  const cudaError_t err = enable_large_smem(sizeof(MelSmem));
+  if (err != cudaSuccess) return err;
+  return noalloc_tile_max(&tile_max);
+}
 
 cudaError_t launch_logmel_noalloc(const float* pcm, int64_t chunks, float* out,
                                   cudaStream_t stream) {

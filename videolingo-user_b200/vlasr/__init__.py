@@ -10,7 +10,7 @@ from ._lib import (VL_BF16, VL_F16, VL_F32, VL_STATUS_BAD_AUDIO, VL_STATUS_BAD_I
                    VlasrInputError, load)
 from .ops import (CHUNK_SAMPLES, MEL_BINS, MEL_FRAMES, add_layernorm, add_rmsnorm,
                   argmax_eos, decode_attention, decode_attention_workspace_bytes, decode_linear,
-                  embed_gather, gelu_erf,
+                  embed_gather, gelu_erf, init,
                   kv_append, logmel, logmel_workspace_bytes, rope_, rope_kv_append, swiglu)
 
 __all__ = [
@@ -18,6 +18,6 @@ __all__ = [
     "SIGNATURES", "VlasrError", "VlasrExecutionError", "VlasrInputError", "load",
     "CHUNK_SAMPLES", "MEL_BINS", "MEL_FRAMES", "add_layernorm", "add_rmsnorm", "argmax_eos",
     "decode_attention", "decode_attention_workspace_bytes", "decode_linear", "embed_gather",
-    "gelu_erf", "kv_append", "logmel", "logmel_workspace_bytes", "rope_", "rope_kv_append",
+    "gelu_erf", "init", "kv_append", "logmel", "logmel_workspace_bytes", "rope_", "rope_kv_append",
     "swiglu",
 ]

@@ -25,6 +25,7 @@ SIGNATURES = {
     "vl_version": (c_int, []),
     "vl_last_error": (ctypes.c_char_p, []),
     "vl_device_count": (c_int, []),
+    "vl_init": (c_int, [c_int]),
     "vl_logmel_workspace_bytes": (c_size_t, [c_int64]),
     "vl_logmel": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "vl_logmel_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),

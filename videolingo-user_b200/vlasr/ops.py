@@ -79,6 +79,20 @@ def _same(ref: torch.Tensor, t: torch.Tensor | None, name: str) -> None:
 # Norms
 # ---------------------------------------------------------------------------
 
+def init(device: torch.device | int | None = None) -> None:
+    """Once-per-device set-up (vl_init): builds the GELU tables and the
+    kernels' attributes ahead of the first op call, e.g. before capturing a
+    CUDA graph.  Optional - every op does its own part on first use."""
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        idx = torch.device(device).index
+        idx = torch.cuda.current_device() if idx is None else idx
+    check(_lib.load().vl_init(int(idx)), "vl_init")
+
+
 def add_layernorm(residual: torch.Tensor, delta: torch.Tensor | None, gamma: torch.Tensor,
                   beta: torch.Tensor | None, eps: float = 1e-5,
                   out: torch.Tensor | None = None) -> torch.Tensor:
