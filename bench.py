@@ -326,6 +326,26 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         return ("K/V [64,4,128] -> 64x4096 slots", 4 * k.numel() * 2,
                 lambda: vlasr.kv_append(k, v, kc, vc, slots))
 
+    def decode_rows_fused():
+        # config 3's three row ops in one launch (vl_decode_rows): add+RMSNorm
+        # [64,2048], RoPE of Q [64,16,128] / K [64,4,128] (rot 64), KV append
+        q, k, v, kc, vc, pos32, slots = decode_inputs()
+        x, r, w = rnd((64, 2048)), rnd((64, 2048)), rnd(2048, 1.0, 0.02)
+        out = torch.empty_like(x)
+        q2, k2, v2 = q.view(64, -1), k.view(64, -1), v.view(64, -1)
+        nbytes = 4 * x.numel() * 2 + (q.numel() + k.numel()) * 2 + 4 * k.numel() * 2
+        return ("add+RMSNorm [64,2048] + RoPE Q [64,16,128] K [64,4,128] rot 64 + KV append, "
+                "one launch", nbytes,
+                lambda: vlasr.decode_rows(r, x, w, q2, k2, v2, kc, vc, pos32, slots,
+                                          head_dim=128, rotary_dim=64, out=out))
+
+    def gelu_large():
+        # the chain's GELU row shape at 200,000 rows (2.05 GB in, 2.05 GB out,
+        # 33x the L2): the launch the DRAM traffic counters are read on
+        gi = rnd((200000, 5120))
+        go = torch.empty_like(gi)
+        return "[200000,5120] bf16", 2 * gi.numel() * 2, lambda: vlasr.gelu_erf(gi, out=go)
+
     def decode_rope_kv_append():
         q, k, v, kc, vc, pos32, slots = decode_inputs()
         return ("fused RoPE + KV append", (q.numel() + 3 * k.numel()) * 2,
@@ -395,6 +415,7 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         return f"{rows} rows x W [{n},{k}] bf16 ({kind})", nbytes, fn
 
     table = [  # name, builder, iterations, latency-bound
+        ("gelu_large", gelu_large, 5, None),  # only with --op (traffic capture)
         ("add_layernorm", add_layernorm, 20, False),
         ("gelu_erf", gelu_erf, 20, False),
         ("embed_gather", embed_gather, 20, False),
@@ -407,6 +428,7 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         ("decode_rope", decode_rope, 20, True),
         ("decode_kv_append", decode_kv_append, 20, True),
         ("decode_rope_kv_append", decode_rope_kv_append, 20, True),
+        ("decode_rows_fused", decode_rows_fused, 20, True),
         ("decode_attention", decode_attention, 20, False),
         ("decode_step_fused", decode_step_fused, 20, False),
         ("decode_attention_engine", decode_attention_engine, 20, False),
@@ -418,6 +440,8 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
     rows = {}
     for name, build, iters, latency in table:
         if only is not None and name != only:
+            continue
+        if only is None and latency is None:
             continue
         config, nbytes, fn = build()
         fn()

@@ -328,6 +328,40 @@ VL_EXPORT int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache,
                       int dtype, int32_t* status, void* stream);
 
 /*
+ * The row ops of a decode step in ONE launch: residual add + RMSNorm of the
+ * hidden rows (as vl_add_rmsnorm), and RoPE of q/k at each token's position
+ * with the KV append (as vl_rope_kv_append).  Replaces the five launches the
+ * reference's decode step spends on them (native/asr/src/decoder.cu:1702-1733:
+ * rope_at_position_map_kernel :471-498, append_kv_mapped_kernel :500-514,
+ * residual_add_kernel :933-938 + cudaMemcpyAsync + rmsnorm_kernel :81-101).
+ *
+ * Norm part (rows may be 0): residual/delta/out [rows][cols], weight [cols];
+ *   h = round(residual + delta) (delta NULL: h = residual); residual := h;
+ *   out = round((h * rsqrt(sum(h^2)/cols + eps)) * weight).
+ * Token part (tokens may be 0): q [tokens][q_row_stride] (n_q_heads *
+ *   head_dim used), k and v [tokens][kv_row_stride] (n_kv_heads * head_dim
+ *   used), caches [num_slots][n_kv_heads * head_dim]; q and k are rotated in
+ *   place at positions[t] (rotate-half on the first rotary_dim dims of every
+ *   head, base `base`), the rotated k row and the v row are stored to slot
+ *   slot_mapping[t] (slot < 0: not cached; slot >= num_slots: not cached and
+ *   VL_STATUS_BAD_SLOT set in *status).
+ * The two parts run side by side, so the norm rows must not overlap q, k or
+ * v (checked).  Each part computes exactly what its own entry point
+ * computes: the same rounding points, the same cos/sin.  Requirements:
+ * 16-byte aligned pointers; cols, head_dim, rotary_dim / 2 and the row
+ * strides multiples of the 16-byte vector (8 for f16/bf16, 4 for f32);
+ * cols at most 1024 vectors.  No allocation, no synchronisation.
+ */
+VL_EXPORT int vl_decode_rows(void* residual, const void* delta, const void* weight, void* out,
+                             int64_t rows, int64_t cols, float eps, void* q, void* k,
+                             const void* v, void* k_cache, void* v_cache,
+                             const int32_t* positions, const int64_t* slot_mapping,
+                             int64_t tokens, int n_q_heads, int n_kv_heads, int head_dim,
+                             int rotary_dim, double base, int64_t q_row_stride,
+                             int64_t kv_row_stride, int64_t num_slots, int dtype,
+                             int32_t* status, void* stream);
+
+/*
  * Launch flags of the decode-step entry points (vl_decode_attention,
  * vl_decode_linear).
  *

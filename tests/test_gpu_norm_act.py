@@ -17,8 +17,10 @@ from helpers import TOL, from_np, normwise, to_np, torch_dtype
 pytestmark = pytest.mark.gpu
 
 DTYPES = ["f32", "f16", "bf16"]
+# Up to 2 rows per SM (296 on a B200) take the block-per-row path, more rows
+# the warp-per-row path; both sides of that boundary are listed.
 NORM_SHAPES = [(1, 1280), (3, 1280), (1500, 1280), (7, 2048), (64, 2048), (5, 7), (2, 1281),
-               (4, 4096), (3, 6000), (2, 64), (9, 520), (1, 8)]
+               (4, 4096), (3, 6000), (2, 64), (9, 520), (1, 8), (296, 2048), (297, 1280)]
 
 
 def _inputs(rows, cols, dtype, seed, weight_mean=1.0):

@@ -203,6 +203,20 @@ def test_kv_append_slot_mapping(dev, dtype):
     assert int((kc != 0).any(-1).any(-1).sum().item()) == int(ok.sum())
 
 
+def test_kv_append_many_tokens_warp_path(dev):
+    """Above 2 tokens per SM the append runs one warp per token (prefill)."""
+    rng = np.random.default_rng(12)
+    tokens, slots = 1000, 4096
+    k = from_np(rng.normal(0, 1, (tokens, 4, 128)), torch.bfloat16, dev)
+    v = from_np(rng.normal(0, 1, (tokens, 4, 128)), torch.bfloat16, dev)
+    kc = torch.zeros(slots, 4, 128, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    slot = torch.from_numpy(rng.permutation(slots)[:tokens].astype(np.int64)).to(dev)
+    vlasr.kv_append(k, v, kc, vc, slot)
+    np.testing.assert_array_equal(_bits(kc[slot]), _bits(k))
+    np.testing.assert_array_equal(_bits(vc[slot]), _bits(v))
+
+
 def test_kv_append_strided_rows(dev):
     """K/V as column slices of a packed QKV buffer (row stride > row width)."""
     rng = np.random.default_rng(9)

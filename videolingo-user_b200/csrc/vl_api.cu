@@ -397,6 +397,86 @@ int vl_rope_kv_append(void* q, void* k, const void* v, void* k_cache, void* v_ca
                      "vl_rope_kv_append");
 }
 
+int vl_decode_rows(void* residual, const void* delta, const void* weight, void* out,
+                   int64_t rows, int64_t cols, float eps, void* q, void* k, const void* v,
+                   void* k_cache, void* v_cache, const int32_t* positions,
+                   const int64_t* slot_mapping, int64_t tokens, int n_q_heads, int n_kv_heads,
+                   int head_dim, int rotary_dim, double base, int64_t q_row_stride,
+                   int64_t kv_row_stride, int64_t num_slots, int dtype, int32_t* status,
+                   void* stream) {
+  const char* op = "vl_decode_rows";
+  if (!valid_dtype(dtype)) return fail(VL_ERR_INVALID, "%s: unsupported dtype %d", op, dtype);
+  const int64_t E = 16 / dtype_size(dtype);
+  if (rows < 0 || tokens < 0 || rows > (int64_t(1) << 30) || tokens > (int64_t(1) << 30))
+    return fail(VL_ERR_INVALID, "%s: rows and tokens must be in [0, 2^30]", op);
+  if (rows > 0) {
+    const int st = check_norm(op, residual, delta, weight, out, rows, cols, eps, dtype);
+    if (st != VL_OK) return st;
+    if (cols % E != 0 || cols / E > 4 * 256)
+      return fail(VL_ERR_INVALID, "%s: cols must be a multiple of %lld and at most %lld", op,
+                  static_cast<long long>(E), static_cast<long long>(4 * 256 * E));
+    if (!vl::aligned16(residual) || !vl::aligned16(weight) || !vl::aligned16(out) ||
+        (delta != nullptr && !vl::aligned16(delta)))
+      return fail(VL_ERR_INVALID, "%s: residual, delta, weight and out must be 16-byte aligned",
+                  op);
+  }
+  if (tokens > 0) {
+    const int st = check_rope(op, q, k, tokens, n_q_heads, n_kv_heads, head_dim, rotary_dim, base,
+                              q_row_stride, kv_row_stride, dtype);
+    if (st != VL_OK) return st;
+    if (n_q_heads <= 0 || n_kv_heads <= 0 || v == nullptr || k_cache == nullptr ||
+        v_cache == nullptr || positions == nullptr || slot_mapping == nullptr)
+      return fail(VL_ERR_INVALID, "%s: q, k, v, caches, positions and slots are all needed", op);
+    if (head_dim % E != 0 || (rotary_dim / 2) % E != 0 || q_row_stride % E != 0 ||
+        kv_row_stride % E != 0)
+      return fail(VL_ERR_INVALID,
+                  "%s: head_dim, rotary_dim / 2 and the row strides must be multiples of %lld",
+                  op, static_cast<long long>(E));
+    if (!vl::aligned16(q) || !vl::aligned16(k) || !vl::aligned16(v) || !vl::aligned16(k_cache) ||
+        !vl::aligned16(v_cache))
+      return fail(VL_ERR_INVALID, "%s: q, k, v and the caches must be 16-byte aligned", op);
+    if (num_slots < 0) return fail(VL_ERR_INVALID, "%s: num_slots must be >= 0", op);
+    if (rows > 0) {
+      const int64_t es = dtype_size(dtype);
+      const int64_t nb = rows * cols * es;
+      const void* norm_bufs[3] = {residual, out, delta};
+      const void* tok_bufs[3] = {q, k, v};
+      const int64_t tok_bytes[3] = {tokens * q_row_stride * es, tokens * kv_row_stride * es,
+                                    tokens * kv_row_stride * es};
+      for (const void* a : norm_bufs)
+        for (int i = 0; i < 3; ++i)
+          if (a != nullptr && overlaps(a, nb, tok_bufs[i], tok_bytes[i]))
+            return fail(VL_ERR_INVALID, "%s: the norm rows must not overlap q, k or v", op);
+    }
+  }
+  vl::DecodeRowsArgs a{};
+  a.residual = residual;
+  a.delta = delta;
+  a.weight = weight;
+  a.out = out;
+  a.rows = rows;
+  a.cols = static_cast<int>(cols);
+  a.eps = eps;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.positions = positions;
+  a.slot_mapping = slot_mapping;
+  a.tokens = tokens;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.rope_base = base;
+  a.q_row_stride = q_row_stride;
+  a.kv_row_stride = kv_row_stride;
+  a.num_slots = num_slots;
+  a.status = status;
+  return exec_status(vl::launch_decode_rows(a, dtype, static_cast<cudaStream_t>(stream)), op);
+}
+
 size_t vl_decode_attention_workspace_bytes(int64_t tokens, int n_q_heads, int n_kv_heads,
                                            int head_dim, int64_t max_seq_len) {
   if (tokens <= 0 || n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads != 0 ||

@@ -9,7 +9,8 @@
 //   append_kv_batched(_dev)_kernel :857-870/:335-351, append_kv_mapped_kernel :500-514
 //       cache[chunk][pos] = k/v row
 // One warp moves one row with the widest access its alignment allows
-// (16-byte vectors for 2048-wide bf16 rows: 8 per lane).  The reference
+// (16-byte vectors for 2048-wide bf16 rows: 8 per lane); a KV append of
+// few tokens takes one block per token instead.  The reference
 // counts placeholders with a serial O(pos) loop for every position; here
 // only placeholder rows count, 32 ids per step with a warp ballot.
 #include "vl_common.cuh"
@@ -115,6 +116,32 @@ __global__ void __launch_bounds__(kRowThreads)
   warp_copy(v_cache + slot * row_bytes, v + t * vs, row_bytes, width, lane);
 }
 
+// Few tokens (a decode step): one block per token, one 16-byte vector of K
+// or V per thread.  The row vectors and the slot are requested together -
+// only the stores depend on the slot - so a launch costs one memory round
+// trip instead of two, and 64 tokens occupy 64 SMs instead of 8.
+__global__ void __launch_bounds__(kRowThreads)
+    kv_append_token_kernel(const char* __restrict__ k, const char* __restrict__ v,
+                           char* k_cache, char* v_cache, const int64_t* __restrict__ slot_mapping,
+                           int vec_per_row, int64_t ks, int64_t vs, int64_t num_slots,
+                           int32_t* status) {
+  const int64_t t = blockIdx.x;
+  const int64_t row_bytes = static_cast<int64_t>(vec_per_row) * 16;
+  for (int i = threadIdx.x; i < 2 * vec_per_row; i += blockDim.x) {
+    const bool is_v = i >= vec_per_row;
+    const int c = is_v ? i - vec_per_row : i;
+    const uint4 val =
+        ld_vec((is_v ? v + t * vs : k + t * ks) + static_cast<int64_t>(c) * 16);
+    const int64_t slot = __ldg(slot_mapping + t);
+    if (slot < 0) continue;
+    if (slot >= num_slots) {
+      if (i == 0 && status) atomicOr(status, VL_STATUS_BAD_SLOT);
+      continue;
+    }
+    st_vec((is_v ? v_cache : k_cache) + slot * row_bytes + static_cast<int64_t>(c) * 16, val);
+  }
+}
+
 int access_width(int64_t a, int64_t b, int64_t c, int64_t d) {
   const int64_t m = a | b | c | d;
   if ((m & 15) == 0) return 16;
@@ -152,6 +179,17 @@ cudaError_t launch_kv_append(const void* k, const void* v, void* k_cache, void* 
       reinterpret_cast<intptr_t>(k) | reinterpret_cast<intptr_t>(v),
       reinterpret_cast<intptr_t>(k_cache) | reinterpret_cast<intptr_t>(v_cache), row_bytes,
       k_row_stride_bytes | v_row_stride_bytes);
+  if (width == 16 && tokens <= 2 * static_cast<int64_t>(sm_count()) &&
+      row_bytes / 16 <= (int64_t(1) << 20)) {
+    const int vpr = static_cast<int>(row_bytes / 16);
+    int threads = ((2 * vpr + 31) / 32) * 32;
+    if (threads > kRowThreads) threads = kRowThreads;
+    kv_append_token_kernel<<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
+        static_cast<const char*>(k), static_cast<const char*>(v), static_cast<char*>(k_cache),
+        static_cast<char*>(v_cache), slot_mapping, vpr, k_row_stride_bytes, v_row_stride_bytes,
+        num_slots, status);
+    return cudaGetLastError();
+  }
   const int64_t blocks = (tokens + kRowThreads / 32 - 1) / (kRowThreads / 32);
   kv_append_kernel<<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
       static_cast<const char*>(k), static_cast<const char*>(v), static_cast<char*>(k_cache),

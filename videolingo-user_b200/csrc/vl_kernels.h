@@ -140,6 +140,37 @@ struct ArgmaxArgs {
 };
 cudaError_t launch_argmax_eos(const ArgmaxArgs& args, int dtype, cudaStream_t stream);
 
+// The row ops of a decode step in one launch (vl_decode_rows.cu): residual
+// add + RMSNorm of `rows` hidden rows, and RoPE of q/k at each token's
+// position with the append of the rotated k and of v to the KV cache.
+struct DecodeRowsArgs {
+  void* residual;            // [rows][cols]
+  const void* delta;         // [rows][cols] or nullptr
+  const void* weight;        // [cols]
+  void* out;                 // [rows][cols]
+  int64_t rows;
+  int cols;
+  float eps;
+  void* q;                   // [tokens][q_row_stride], n_q_heads * head_dim used
+  void* k;                   // [tokens][kv_row_stride], n_kv_heads * head_dim used
+  const void* v;             // [tokens][kv_row_stride]
+  void* k_cache;             // [num_slots][n_kv_heads * head_dim]
+  void* v_cache;
+  const int32_t* positions;  // [tokens]
+  const int64_t* slot_mapping;  // [tokens]
+  int64_t tokens;
+  int n_q_heads;
+  int n_kv_heads;
+  int head_dim;
+  int rotary_dim;
+  double rope_base;
+  int64_t q_row_stride;
+  int64_t kv_row_stride;
+  int64_t num_slots;
+  int32_t* status;
+};
+cudaError_t launch_decode_rows(const DecodeRowsArgs& args, int dtype, cudaStream_t stream);
+
 // Once-per-device set-up done ahead of the first op call (vl_init): the
 // GELU tables (a private stream, one kernel, one stream synchronise) and the
 // log-mel kernel's shared-memory limit and scratch address.

@@ -13,7 +13,8 @@
 // reads residual and delta once and writes the new residual and the
 // normalised row once (4 row transfers instead of 7).
 //
-// Layout: one warp owns one row.  The row is held in registers as packed
+// Layout: one warp owns one row (few-row launches: one block per row, see
+// vl_rows.cuh).  The row is held in registers as packed
 // 16-byte vectors (NV per lane), the moments are reduced with warp shuffles
 // (no shared memory, no block barrier), and the output pass re-reads only the
 // L1/L2-resident gamma/beta.  Rows that do not fit the register path (length
@@ -21,11 +22,16 @@
 // lane) take a block-per-row fallback that streams the row twice.
 #include "vl_common.cuh"
 #include "vl_kernels.h"
+#include "vl_rows.cuh"
 
 namespace vl {
 namespace {
 
 constexpr int kNormThreads = 256;  // 8 rows per block
+// Up to this many rows per SM take the block-per-row path: a launch of that
+// size is latency-bound (one memory round trip), and spreading the rows over
+// more SMs shortens it; above it the warp-per-row stream is the faster one.
+constexpr int kFewRowsPerSm = 2;
 
 template <typename T, int NV, bool kDelta, bool kRms>
 __global__ void __launch_bounds__(kNormThreads)
@@ -183,6 +189,33 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// Few rows (a decode step): one block per row (vl_rows.cuh), so 64 rows run
+// on 64 SMs with the norm weights fetched alongside the row.
+template <typename T, int NV, bool kDelta, bool kRms>
+__global__ void __launch_bounds__(kRowBlockThreads)
+    add_norm_row_kernel(T* residual, const T* delta, const T* __restrict__ gamma,
+                        const T* __restrict__ beta, T* out, int cols, float eps) {
+  __shared__ float red[2 * kRowBlockThreads / 32];
+  add_norm_row_block<T, NV, kDelta, kRms>(residual, delta, gamma, beta, out, blockIdx.x, cols,
+                                          eps, red);
+}
+
+template <typename T, int NV, bool kRms>
+cudaError_t launch_row(void* residual, const void* delta, const void* gamma, const void* beta,
+                       void* out, int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  if (delta)
+    add_norm_row_kernel<T, NV, true, kRms><<<static_cast<unsigned>(rows), kRowBlockThreads, 0,
+                                             stream>>>(
+        static_cast<T*>(residual), static_cast<const T*>(delta), static_cast<const T*>(gamma),
+        static_cast<const T*>(beta), static_cast<T*>(out), static_cast<int>(cols), eps);
+  else
+    add_norm_row_kernel<T, NV, false, kRms><<<static_cast<unsigned>(rows), kRowBlockThreads, 0,
+                                              stream>>>(
+        static_cast<T*>(residual), nullptr, static_cast<const T*>(gamma),
+        static_cast<const T*>(beta), static_cast<T*>(out), static_cast<int>(cols), eps);
+  return cudaGetLastError();
+}
+
 template <typename T, int NV, bool kRms>
 cudaError_t launch_warp(void* residual, const void* delta, const void* gamma, const void* beta,
                         void* out, int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
@@ -207,6 +240,14 @@ cudaError_t dispatch(void* residual, const void* delta, const void* gamma, const
                       aligned16(gamma) && (delta == nullptr || aligned16(delta)) &&
                       (beta == nullptr || aligned16(beta));
   const int64_t per_lane = (cols / E + 31) / 32;
+  const int64_t per_thread = (cols / E + kRowBlockThreads - 1) / kRowBlockThreads;
+  if (vec_ok && rows <= kFewRowsPerSm * sm_count() && per_thread <= 4) {
+    switch (per_thread) {
+      case 1: return launch_row<T, 1, kRms>(residual, delta, gamma, beta, out, rows, cols, eps, stream);
+      case 2: return launch_row<T, 2, kRms>(residual, delta, gamma, beta, out, rows, cols, eps, stream);
+      default: return launch_row<T, 4, kRms>(residual, delta, gamma, beta, out, rows, cols, eps, stream);
+    }
+  }
   if (vec_ok && per_lane <= 16) {
     switch (per_lane) {
       case 1: return launch_warp<T, 1, kRms>(residual, delta, gamma, beta, out, rows, cols, eps, stream);

@@ -10,6 +10,7 @@ from ._lib import (VL_BF16, VL_F16, VL_F32, VL_STATUS_BAD_AUDIO, VL_STATUS_BAD_I
                    VlasrInputError, load)
 from .ops import (CHUNK_SAMPLES, MEL_BINS, MEL_FRAMES, add_layernorm, add_rmsnorm,
                   argmax_eos, decode_attention, decode_attention_workspace_bytes, decode_linear,
+                  decode_rows,
                   embed_gather, gelu_erf, init,
                   kv_append, logmel, logmel_workspace_bytes, rope_, rope_kv_append, swiglu)
 
@@ -17,7 +18,7 @@ __all__ = [
     "VL_BF16", "VL_F16", "VL_F32", "VL_STATUS_BAD_AUDIO", "VL_STATUS_BAD_ID", "VL_STATUS_BAD_SLOT",
     "SIGNATURES", "VlasrError", "VlasrExecutionError", "VlasrInputError", "load",
     "CHUNK_SAMPLES", "MEL_BINS", "MEL_FRAMES", "add_layernorm", "add_rmsnorm", "argmax_eos",
-    "decode_attention", "decode_attention_workspace_bytes", "decode_linear", "embed_gather",
+    "decode_attention", "decode_attention_workspace_bytes", "decode_linear", "decode_rows", "embed_gather",
     "gelu_erf", "init", "kv_append", "logmel", "logmel_workspace_bytes", "rope_", "rope_kv_append",
     "swiglu",
 ]

@@ -47,6 +47,10 @@ SIGNATURES = {
     "vl_rope_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_int64, c_int, c_int, c_int, c_int, c_double, c_int64,
                                   c_int, c_void_p, c_void_p]),
+    "vl_decode_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_int64, c_int, c_int, c_int, c_int, c_double, c_int64,
+                               c_int64, c_int64, c_int, c_void_p, c_void_p]),
     "vl_decode_attention_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64]),
     "vl_decode_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
                                  c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int,

@@ -299,6 +299,55 @@ def rope_kv_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: t
           "vl_rope_kv_append")
 
 
+def decode_rows(residual: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor,
+                q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                v_cache: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor, *,
+                head_dim: int, rotary_dim: int | None = None, base: float = 10000.0,
+                eps: float = 1e-5, out: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> torch.Tensor:
+    """The row ops of a decode step in one launch (vl_decode_rows): residual
+    add + RMSNorm of `residual` [rows, cols] (as add_rmsnorm) and, side by
+    side, RoPE of q/k at `positions` with the KV append at `slot_mapping`
+    (as rope_kv_append).  q [tokens, n_q*head_dim], k/v [tokens,
+    n_kv*head_dim] (contiguous rows), caches [num_slots, n_kv, head_dim].
+    Returns the normalised rows."""
+    rotary_dim = head_dim if rotary_dim is None else rotary_dim
+    _contig(residual, "residual")
+    if residual.dim() != 2:
+        raise VlasrInputError("residual must be [rows, cols]")
+    rows, cols = residual.shape
+    for name, t in (("delta", delta), ("weight", weight), ("q", q), ("k", k), ("v", v),
+                    ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t is not None:
+            _contig(t, name)
+            _same(residual, t, name)
+    if out is None:
+        out = torch.empty_like(residual)
+    _contig(out, "out")
+    _same(residual, out, "out")
+    tokens = positions.numel()
+    if q.dim() != 2 or k.dim() != 2 or v.shape != k.shape or q.shape[0] != tokens:
+        raise VlasrInputError("q must be [tokens, n_q*head_dim], k and v [tokens, n_kv*head_dim]")
+    if q.shape[1] % head_dim or k.shape[1] % head_dim:
+        raise VlasrInputError("q/k widths must be multiples of head_dim")
+    nq, nk = q.shape[1] // head_dim, k.shape[1] // head_dim
+    if k_cache.shape != v_cache.shape or k_cache.numel() % (nk * head_dim):
+        raise VlasrInputError("k_cache/v_cache must be [num_slots, n_kv, head_dim]")
+    num_slots = k_cache.numel() // (nk * head_dim)
+    _contig(positions, "positions")
+    _contig(slot_mapping, "slot_mapping")
+    if positions.dtype != torch.int32 or slot_mapping.dtype != torch.int64:
+        raise VlasrInputError("positions must be int32 and slot_mapping int64")
+    if slot_mapping.numel() != tokens:
+        raise VlasrInputError("slot_mapping must have one entry per token")
+    check(_lib.load().vl_decode_rows(
+        _ptr(residual), _ptr(delta), _ptr(weight), _ptr(out), rows, cols, float(eps), _ptr(q),
+        _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(slot_mapping),
+        tokens, nq, nk, head_dim, rotary_dim, float(base), q.shape[1], k.shape[1], num_slots,
+        _dtype_code(residual), _ptr(status), _stream(residual)), "vl_decode_rows")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Decode-step attention
 # ---------------------------------------------------------------------------
