@@ -45,6 +45,16 @@ METRIC = "audio-seconds/s (log-mel + 32 x fused add+LayerNorm & GELU per 30 s ch
 FALLBACK_HBM_GBS = 6650.0
 
 
+GATHER_TEXT = {
+    "copy": (" + all-gather of each step's outputs by copy-engine pushes into every rank's "
+             "buffer over NVLink (no kernels), overlapped with the next step; one NCCL "
+             "barrier at the end (inside the timed region)"),
+    "nccl": (" + NCCL all-gather of each step's outputs, overlapped with the next step on a "
+             "side stream (the last one inside the timed region)"),
+    "blocking": " + NCCL all-gather of each step's outputs at the end of the step",
+}
+
+
 def parse() -> argparse.Namespace:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -58,9 +68,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--nccl-channels", type=int, default=None,
                    help="cap NCCL's channels (and so the SMs its all-gather occupies "
                         "while it overlaps the next step's kernels)")
-    p.add_argument("--gather", choices=["overlap", "blocking"], default="overlap",
-                   help="all-gather each step's outputs on a side stream overlapping the "
-                        "next step (default) or on the compute stream at the end of the step")
+    p.add_argument("--gather", choices=["copy", "nccl", "blocking"], default="copy",
+                   help="all-gather of each step's outputs: copy-engine pushes into every "
+                        "rank's buffer overlapping the next step (default), an NCCL all-gather "
+                        "on a side stream overlapping the next step, or NCCL at the end of "
+                        "the step")
     p.add_argument("--encoder", action="store_true",
                    help="encoder mode: the GLM-ASR audio tower + projector (vlasr.encoder) on a "
                         "seeded synthetic checkpoint; with --impl reference, the reference's own "
@@ -995,7 +1007,7 @@ def main() -> None:
     shape = ChainShape(chunks=c1 - c0, layers=LAYERS)
     group = None
     chain = EncoderNormChain(shape, dev, seed=0, group=group, world=world, rank=rank,
-                             total_chunks=args.chunks, overlap_gather=args.gather == "overlap")
+                             total_chunks=args.chunks, gather=args.gather)
     pcm = audio_chunks_device(shape.chunks, c0, 0, dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -1095,6 +1107,7 @@ def main() -> None:
                "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)"}
         del pcm_host, mel_host, y_host, pcm_dev
 
+    chain.close()
     del chain, pcm
     torch.cuda.empty_cache()
     ops = None
@@ -1115,12 +1128,8 @@ def main() -> None:
             "config": {"workload": "config 4: box-scale chunk sharding", "chunks": args.chunks,
                        "chunks_per_rank": shape.chunks, "layers": LAYERS,
                        "ln_shape": [1500, 1280], "gelu_shape": [1500, 5120],
-                       "parallelism": f"chunk-sharded x{world}" + (
-                           (" + NCCL all-gather of each step's outputs, overlapped with the next "
-                            "step on a side stream (the last one inside the timed region)")
-                           if args.gather == "overlap" else
-                           " + NCCL all-gather of each step's outputs at the end of the step"
-                           ) if world > 1 else "",
+                       "parallelism": f"chunk-sharded x{world}" + GATHER_TEXT[args.gather]
+                       if world > 1 else "",
                        "l2": "inputs larger than L2 (each op streams >= 0.49 GB per launch)",
                        "nccl_max_nchannels": os.environ.get("NCCL_MAX_NCHANNELS"),
                        "bytes_per_step": bytes_step["total"] * world},

@@ -121,6 +121,35 @@ VL_EXPORT int vl_device_count(void);
 VL_EXPORT int vl_init(int device);
 
 /* ------------------------------------------------------------------------ */
+/* Peer memory for the chunk-sharded pipeline                                */
+/* ------------------------------------------------------------------------ */
+/*
+ * The multi-GPU run of the layer chain shards chunks over one process per
+ * GPU and then gives every rank all ranks' encoder-norm outputs.  These four
+ * calls let a host do that exchange with the GPUs' copy engines over
+ * NVLink - no kernel, so the shard transfers take no SM time from the layer
+ * kernels that run beside them.  They have no counterpart in the reference,
+ * whose engine runs on one GPU (native/asr/src/engine.cu:1166-1616).
+ *
+ * vl_ipc_export: CUDA IPC handle (VL_IPC_HANDLE_BYTES opaque bytes) of the
+ *   device allocation that contains `ptr`, and ptr's byte offset in it.
+ * vl_ipc_open: maps another process's exported allocation into this one
+ *   (on the current device; peer access is enabled on first use) and
+ *   returns its base address; add the exported offset.
+ * vl_ipc_close: unmaps an address vl_ipc_open returned.
+ * vl_copy_async: cudaMemcpyAsync device-to-device of `bytes` on `stream`;
+ *   src or dst may be a mapped peer address.  They must not overlap.
+ * The host orders the copies against the producer's kernels (e.g. a
+ * collective barrier on the copying stream); these calls do no ordering of
+ * their own.
+ */
+#define VL_IPC_HANDLE_BYTES 64
+VL_EXPORT int vl_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+VL_EXPORT int vl_ipc_open(const void* handle, void** base_out);
+VL_EXPORT int vl_ipc_close(void* base);
+VL_EXPORT int vl_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Log-mel frontend                                                          */
 /* ------------------------------------------------------------------------ */
 

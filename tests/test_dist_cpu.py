@@ -163,3 +163,72 @@ def test_sharded_engine_returns_every_chunk_in_order(chunks):
     for p in procs:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in results), results
+
+
+# ---------------------------------------------------------------------------
+# Copy-engine all-gather (PeerPushGather): the host side of the handle
+# exchange and the copy plan, with the CUDA IPC calls replaced by a fake.
+# ---------------------------------------------------------------------------
+
+def test_push_plan_writes_own_slot_of_every_rank():
+    from vlasr.pipeline import push_plan
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            plan = push_plan(world, rank, 1000)
+            assert [j for j, _ in plan] == [rank] + [j for j in range(world) if j != rank]
+            assert all(off == rank * 1000 for _, off in plan)
+
+
+class _FakeIpc:
+    """Handles name (rank, offset); opening one gives base 1_000_000 * (rank + 1)."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened, self.closed = [], []
+
+    def export(self, ptr):
+        return (f"rank{self.rank}".encode().ljust(64, b"\0"), 64 * (self.rank + 1))
+
+    def open(self, handle):
+        peer = int(handle.rstrip(b"\0")[4:])
+        assert peer != self.rank
+        base = 1_000_000 * (peer + 1)
+        self.opened.append(base)
+        return base
+
+    def close(self, base):
+        self.closed.append(base)
+
+
+def _peer_worker(rank, world, port, q):
+    try:
+        from vlasr.pipeline import PeerPushGather
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=30))
+        full = torch.zeros(world * 4, 8)
+        ipc = _FakeIpc(rank)
+        g = PeerPushGather(full, 4 * 8 * 4, None, world, rank, ipc=ipc)
+        dest = list(g.dest)
+        g.close()
+        expect = [full.data_ptr() if j == rank else 1_000_000 * (j + 1) + 64 * (j + 1)
+                  for j in range(world)]
+        ok = dest == expect and sorted(ipc.closed) == sorted(ipc.opened) and \
+            len(ipc.opened) == world - 1 and g.opened == []
+        dist.destroy_process_group()
+        q.put((rank, ok, None if ok else (dest, expect)))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, False, repr(exc)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_gather_maps_every_other_rank_once(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in results), results

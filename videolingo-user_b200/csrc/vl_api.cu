@@ -134,6 +134,32 @@ int vl_init(int device) {
   return exec_status(err, "vl_init");
 }
 
+int vl_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_ipc_export: null pointer");
+  return exec_status(vl::ipc_export(ptr, handle_out, offset_out), "vl_ipc_export");
+}
+
+int vl_ipc_open(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr)
+    return fail(VL_ERR_INVALID, "vl_ipc_open: null pointer");
+  return exec_status(vl::ipc_open(handle, base_out), "vl_ipc_open");
+}
+
+int vl_ipc_close(void* base) {
+  if (base == nullptr) return fail(VL_ERR_INVALID, "vl_ipc_close: null pointer");
+  return exec_status(vl::ipc_close(base), "vl_ipc_close");
+}
+
+int vl_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return ok();
+  if (dst == nullptr || src == nullptr) return fail(VL_ERR_INVALID, "vl_copy_async: null pointer");
+  if (overlaps(dst, static_cast<int64_t>(bytes), src, static_cast<int64_t>(bytes)))
+    return fail(VL_ERR_INVALID, "vl_copy_async: source and destination overlap");
+  return exec_status(vl::copy_async(dst, src, bytes, static_cast<cudaStream_t>(stream)),
+                     "vl_copy_async");
+}
+
 size_t vl_logmel_workspace_bytes(int64_t chunks) {
   if (chunks <= 0 || chunks > kMaxMelChunks) return 0;
   return vl::logmel_workspace_bytes(chunks);

@@ -171,6 +171,12 @@ struct DecodeRowsArgs {
 };
 cudaError_t launch_decode_rows(const DecodeRowsArgs& args, int dtype, cudaStream_t stream);
 
+// Peer-memory plumbing of the sharded pipeline (vl_peer.cu).
+cudaError_t ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+cudaError_t ipc_open(const void* handle, void** base_out);
+cudaError_t ipc_close(void* base);
+cudaError_t copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
 // Once-per-device set-up done ahead of the first op call (vl_init): the
 // GELU tables (a private stream, one kernel, one stream synchronise) and the
 // log-mel kernel's shared-memory limit and scratch address.

@@ -19,6 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libvlasr.so"
 VL_OK, VL_ERR_EXEC, VL_ERR_INVALID = 0, 1, 2
 VL_F32, VL_F16, VL_BF16 = 0, 1, 2
 VL_STATUS_BAD_ID, VL_STATUS_BAD_AUDIO, VL_STATUS_BAD_SLOT = 1, 2, 4
+VL_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).
 SIGNATURES = {
@@ -26,6 +27,10 @@ SIGNATURES = {
     "vl_last_error": (ctypes.c_char_p, []),
     "vl_device_count": (c_int, []),
     "vl_init": (c_int, [c_int]),
+    "vl_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "vl_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "vl_ipc_close": (c_int, [c_void_p]),
+    "vl_copy_async": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vl_logmel_workspace_bytes": (c_size_t, [c_int64]),
     "vl_logmel": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "vl_logmel_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),

@@ -69,6 +69,113 @@ def gather_outputs(full: torch.Tensor, shard: torch.Tensor, group=None) -> None:
     dist.all_gather_into_tensor(full, shard.contiguous(), group=group)
 
 
+def push_plan(world: int, rank: int, shard_bytes: int) -> list[tuple[int, int]]:
+    """(destination rank, byte offset in its full buffer) of each copy rank
+    `rank` makes per step: its shard goes to its own slot of every rank's
+    full buffer, its own first."""
+    order = [rank] + [j for j in range(world) if j != rank]
+    return [(j, rank * shard_bytes) for j in order]
+
+
+class LibIpc:
+    """The C ABI's peer-memory calls (vl_ipc_export / _open / _close,
+    vl_copy_async) with Python types."""
+
+    def __init__(self):
+        from . import _lib
+        self._lib = _lib
+        self.lib = _lib.load()
+
+    def export(self, ptr: int) -> tuple[bytes, int]:
+        import ctypes
+        handle = (ctypes.c_char * self._lib.VL_IPC_HANDLE_BYTES)()
+        offset = ctypes.c_uint64()
+        self._lib.check(self.lib.vl_ipc_export(ctypes.c_void_p(ptr), handle, ctypes.byref(offset)),
+                        "vl_ipc_export")
+        return bytes(handle), int(offset.value)
+
+    def open(self, handle: bytes) -> int:
+        import ctypes
+        base = ctypes.c_void_p()
+        self._lib.check(self.lib.vl_ipc_open(handle, ctypes.byref(base)), "vl_ipc_open")
+        return int(base.value)
+
+    def close(self, base: int) -> None:
+        self.lib.vl_ipc_close(base)
+
+    def copy(self, dst: int, src: int, nbytes: int, stream: int) -> None:
+        self._lib.check(self.lib.vl_copy_async(dst, src, nbytes, stream), "vl_copy_async")
+
+
+class PeerPushGather:
+    """All-gather of equal row shards with the GPUs' copy engines.
+
+    Every rank maps every other rank's full output buffer once (CUDA IPC
+    through vl_ipc_export / vl_ipc_open) and, each step, copies its own shard
+    into its slot of every rank's buffer (vl_copy_async, one stream per
+    destination), so no kernel and no SM takes part in the exchange.  A
+    rank's copies only read its own finished shard and only write its own
+    slot elsewhere, so a step needs no cross-rank ordering; `barrier()` - a
+    one-element all-reduce on the caller's stream - is the point after which
+    every rank's copies into this rank's buffer are complete.  `ipc`
+    replaces the C ABI calls (tests)."""
+
+    def __init__(self, full: torch.Tensor, shard_bytes: int, group, world: int, rank: int,
+                 ipc=None):
+        import torch.distributed as dist
+        self.ipc = ipc if ipc is not None else LibIpc()
+        self.full = full
+        self.shard_bytes = shard_bytes
+        self.group, self.world, self.rank = group, world, rank
+        records = [None] * world
+        dist.all_gather_object(records, self.ipc.export(full.data_ptr()), group=group)
+        self.dest = [0] * world
+        self.opened = []
+        for j, (handle, offset) in enumerate(records):
+            if j == rank:
+                self.dest[j] = full.data_ptr()
+                continue
+            base = self.ipc.open(handle)
+            self.opened.append(base)
+            self.dest[j] = base + offset
+        self.streams = None
+        self.flag = torch.zeros(1, dtype=torch.int32, device=full.device)
+
+    def push(self, shard: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        """Copy `shard` (this rank's rows, ready on `stream`) into every rank's
+        full buffer; `stream` waits for all the copies."""
+        if shard.numel() * shard.element_size() != self.shard_bytes or not shard.is_contiguous():
+            raise ValueError("shard must be contiguous and shard_bytes long")
+        if self.streams is None:
+            self.streams = [torch.cuda.Stream(self.full.device) for _ in range(self.world)]
+        start = torch.cuda.Event()
+        start.record(stream)
+        for j, off in push_plan(self.world, self.rank, self.shard_bytes):
+            s = self.streams[j]
+            s.wait_event(start)
+            self.ipc.copy(self.dest[j] + off, shard.data_ptr(), self.shard_bytes, s.cuda_stream)
+            done = torch.cuda.Event()
+            done.record(s)
+            stream.wait_event(done)
+
+    def barrier(self, stream: torch.cuda.Stream) -> None:
+        """Order `stream` after every rank's copies enqueued so far."""
+        import torch.distributed as dist
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self.flag, group=self.group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, once every rank has finished its copies."""
+        import torch.distributed as dist
+        if self.full.is_cuda:
+            torch.cuda.synchronize(self.full.device)
+        dist.barrier(group=self.group)
+        for base in self.opened:
+            self.ipc.close(base)
+        self.opened = []
+        dist.barrier(group=self.group)
+
+
 def host_group_bounds(chunks: int, groups: int) -> list[tuple[int, int]]:
     """Chunk groups of the host-buffer pipeline: `groups` equal middle groups
     plus a half-size first and last group, so the upload that nothing
@@ -93,15 +200,24 @@ def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
 class EncoderNormChain:
     """Resident buffers and launch sequence of one rank's shard."""
 
+    GATHERS = ("copy", "nccl", "blocking")
+
     def __init__(self, shape: ChainShape, device, seed: int = 0, group=None, world: int = 1,
-                 rank: int = 0, total_chunks: int | None = None, overlap_gather: bool = True):
+                 rank: int = 0, total_chunks: int | None = None, gather: str = "copy"):
+        """gather (world > 1): "copy" - copy-engine pushes of each step's
+        outputs into every rank's buffer, overlapped with the next step
+        (PeerPushGather); "nccl" - NCCL all_gather_into_tensor on a side
+        stream, overlapped; "blocking" - NCCL at the end of each step."""
+        if gather not in self.GATHERS:
+            raise ValueError(f"gather must be one of {self.GATHERS}")
         self.shape = shape
         self.device = torch.device(device)
         self.group = group
         self.world = world
         self.rank = rank
         self.total_chunks = total_chunks if total_chunks is not None else shape.chunks * world
-        self.overlap_gather = overlap_gather
+        self.gather = gather
+        self.overlap_gather = gather != "blocking"
         s = shape
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed * 7919 + rank)
@@ -130,11 +246,16 @@ class EncoderNormChain:
                                   dtype=torch.uint8)
         self.y_all = None
         self.comm = None
+        self.peers = None
         self.gather_done = [None, None]
         if world > 1:
             self.y_all = torch.empty((self.total_chunks * s.frames, s.hidden), device=self.device,
                                      dtype=bf)
             self.comm = torch.cuda.Stream(self.device)
+            if gather == "copy":
+                if self.total_chunks != s.chunks * world:
+                    raise ValueError("the copy gather needs equal shards")
+                self.peers = PeerPushGather(self.y_all, s.rows * s.hidden * 2, group, world, rank)
 
     @property
     def y(self) -> torch.Tensor:
@@ -164,8 +285,12 @@ class EncoderNormChain:
         ops.gelu_erf(self.g_in[r0:r1], out=self.g_out[r0:r1])
 
     def all_gather(self) -> None:
-        """Blocking all-gather of this step's outputs on the current stream."""
-        if self.y_all is not None:
+        """All-gather of this step's outputs, ordered on the current stream."""
+        if self.y_all is None:
+            return
+        if self.peers is not None:
+            self.peers.push(self.y, torch.cuda.current_stream(self.device))
+        else:
             gather_outputs(self.y_all, self.y, self.group)
 
     def _begin_step(self) -> None:
@@ -197,11 +322,21 @@ class EncoderNormChain:
             self.cur = 1 - self.cur
 
     def finish(self) -> None:
-        """Make the current stream wait for every outstanding all-gather."""
+        """Make the current stream wait for every outstanding all-gather (with
+        the copy gather: for every rank's copies into this rank's y_all).
+        Collective when world > 1: every rank calls it at the same point."""
         cur = torch.cuda.current_stream(self.device)
         for ev in self.gather_done:
             if ev is not None:
                 cur.wait_event(ev)
+        if self.peers is not None:
+            self.peers.barrier(cur)
+
+    def close(self) -> None:
+        """Release the peer mappings of the copy gather (collective)."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def step(self, pcm: torch.Tensor, timer=None) -> None:
         """One pass over this rank's chunks with device-resident PCM.
