@@ -203,6 +203,23 @@ def barrier(world):
         dist.barrier()
 
 
+def host_wait(world: int, rank: int, key: str) -> None:
+    """Rank 0 sets `key` in the process group's store; the other ranks poll
+    it with sleeps (no collective, no busy CPU) until it is set."""
+    if world == 1:
+        return
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
+    if rank == 0:
+        store.set(key, "1")
+        return
+    deadline = time.time() + 280
+    while not store.check([key]):
+        if time.time() > deadline:
+            raise RuntimeError(f"rank 0 did not set {key} in time")
+        time.sleep(0.2)
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -226,6 +243,24 @@ def sum_over_ranks(x: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 # per-op table (configs 1-3 and the mel at 256 chunks), rank 0 only
 # ---------------------------------------------------------------------------
+
+def e2e_breakdown(trace, h2d_bytes: int, d2h_bytes: int, world: int) -> dict:
+    """Per-stream busy time (ms) of one traced host-buffer step and the
+    PCIe rates it implies, max over ranks: `h2d`/`d2h` sum the copy
+    durations on the upload/download streams, `compute` the group
+    computations, `span` runs from the first upload to the last download."""
+    busy = {"h2d": 0.0, "compute": 0.0, "d2h": 0.0}
+    for kind, a, b in trace:
+        busy[kind] += a.elapsed_time(b)
+    span = trace[0][1].elapsed_time(trace[-1][2]) if trace else 0.0
+    out = {k: round(max_over_ranks(v, world), 3) for k, v in busy.items()}
+    out["span"] = round(max_over_ranks(span, world), 3)
+    out["h2d_gbs_per_gpu"] = round(h2d_bytes / (out["h2d"] * 1e-3) / 1e9, 1) if out["h2d"] else None
+    out["d2h_gbs_per_gpu"] = round(d2h_bytes / (out["d2h"] * 1e-3) / 1e9, 1) if out["d2h"] else None
+    out["note"] = ("one traced step after the timed ones; busy = sum of event-pair durations "
+                   "per stream, max over ranks; GB/s = this rank's bytes / its busy time")
+    return out
+
 
 def time_op(fn, iters: int, flush=None) -> float:
     """Mean device time (ms) of fn over `iters` launches, L2 flushed before each.
@@ -1100,11 +1135,20 @@ def main() -> None:
         barrier(world)
         e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
         h2d, d2h = chain.host_bytes_per_step()
+        # one more traced step (outside the timed region): per-stream busy
+        # time of the uploads, the group computations and the downloads
+        trace = []
+        barrier(world)
+        chain.step_host(pcm_host, mel_host, y_host, pcm_dev, groups=groups, trace=trace)
+        chain.finish()
+        torch.cuda.synchronize()
+        barrier(world)
         e2e = {"value": round(audio_s / (e_ms / 1e3), 1), "unit": "audio-s/s",
                "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
                "groups": len(host_group_bounds(shape.chunks, groups)),
-               "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)"}
+               "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)",
+               "breakdown": e2e_breakdown(trace, h2d, d2h, world)}
         del pcm_host, mel_host, y_host, pcm_dev
 
     chain.close()
@@ -1112,11 +1156,16 @@ def main() -> None:
     torch.cuda.empty_cache()
     ops = None
     cpu = None
-    if rank == 0 and world == 1:
-        if not args.no_ops:
-            ops = op_table(peak)
-        if not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_ops:
+        ops = op_table(peak)
+    if not args.no_cpu:
+        # the reference CPU path on this box's host cores, at every N (rank 0
+        # runs it after the GPU timing; the other ranks wait in a host-side
+        # poll of the store, not in a spinning collective, so they leave the
+        # cores to it)
+        if rank == 0:
             cpu = cpu_baseline()
+        host_wait(world, rank, "cpu_baseline_done")
     barrier(world)
 
     if rank == 0:

@@ -485,6 +485,13 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
  * norm_weight 16-byte aligned with row strides that are multiples of 8 elements, x not
  * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
  * flags: 0 or VL_LAUNCH_PDL.
+ * Kernels: when the output columns (n, or n/2 for SWIGLU) are a multiple of
+ * 128, the 5th-generation tensor cores compute it (tcgen05.mma with the
+ * accumulator in tensor memory, weights streamed by TMA, K split over a
+ * thread-block cluster whose partial sums meet in distributed shared
+ * memory); other shapes use a tensor-core kernel of the previous generation
+ * (mma.sync).  Both keep the rounding points above; their fp32 summation
+ * orders differ, each is deterministic.
  */
 #define VL_LINEAR_STORE 0
 #define VL_LINEAR_SWIGLU 1
@@ -496,6 +503,15 @@ VL_EXPORT int vl_decode_linear(const void* x, int64_t x_row_stride, const void* 
                                const void* w, int64_t n, int64_t k, void* y,
                                int64_t y_row_stride, float* ssq_out, int64_t rows,
                                int epilogue, int dtype, int flags, void* stream);
+
+/*
+ * Number of waits of the tensor-core vl_decode_linear kernel on the current
+ * device that gave up (each is bounded to a few seconds; on expiry the kernel
+ * writes NaN for the outputs of the tile it could not finish, releases its
+ * resources and returns instead of hanging).  0 in normal operation.  Reads
+ * a device counter with a synchronous copy.
+ */
+VL_EXPORT int vl_decode_linear_timeouts(uint32_t* count);
 
 /*
  * Decode-step tail: the greedy next token of each row with the EOS freeze,

@@ -184,3 +184,64 @@ def test_pdl_chain_is_bit_identical(dev):
         assert torch.equal(eager[key], plain[key]), key
         assert torch.equal(graphed[key], plain[key]), key
     del graph
+
+
+@pytest.mark.parametrize("epilogue,n", [("store", 528), ("store", 16), ("swiglu", 12320),
+                                        ("residual", 2064)])
+def test_shapes_outside_the_tensor_core_tiles(dev, epilogue, n):
+    """Output widths that are not a multiple of 128 columns take the
+    mma.sync kernel; same references."""
+    rows, k = 9, 2048
+    x = _rand((rows, k), dev, torch.bfloat16, 40 + n)
+    w = _rand((n, k), dev, torch.bfloat16, 41 + n, k ** -0.5)
+    acc = x.float() @ w.float().t()
+    if epilogue == "store":
+        y = vlasr.decode_linear(x, w)
+        ref = _r(acc, torch.bfloat16)
+    elif epilogue == "swiglu":
+        y = vlasr.decode_linear(x, w, epilogue="swiglu")
+        g, u = _r(acc[:, :n // 2], torch.bfloat16), _r(acc[:, n // 2:], torch.bfloat16)
+        ref = _r(g / (1 + torch.exp(-g)) * u, torch.bfloat16)
+    else:
+        h = _rand((rows, n), dev, torch.bfloat16, 42)
+        ref = _r(h.float() + _r(acc, torch.bfloat16), torch.bfloat16)
+        y = vlasr.decode_linear(x, w, epilogue="residual", out=h)
+    torch.cuda.synchronize()
+    assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("rows", [1, 16, 17, 32, 33, 64])
+def test_tensor_core_row_paddings_all_epilogues(dev, rows):
+    """16 / 32 / 64-row MMA tiles (N of the swapped product) at their edges,
+    every epilogue, the decoder's widths."""
+    hid, ffn = 2048, 6144
+    x = _rand((rows, hid), dev, torch.bfloat16, 50 + rows)
+    m = _rand((rows, ffn), dev, torch.bfloat16, 51 + rows)
+    gamma = _rand(hid, dev, torch.bfloat16, 52, 0.02) + 1
+    w_gu = _rand((2 * ffn, hid), dev, torch.bfloat16, 53, hid ** -0.5)
+    w_d = _rand((hid, ffn), dev, torch.bfloat16, 54, ffn ** -0.5)
+    xs = x.float().view(rows, hid // 16, 16)
+    ssq = (xs * xs).sum(-1).t().contiguous()
+    y = vlasr.decode_linear(x, w_gu, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
+    xn = _norm_ref(x, gamma, (x.float() ** 2).sum(-1), hid, torch.bfloat16)
+    gu = xn @ w_gu.float().t()
+    g, u = _r(gu[:, :ffn], torch.bfloat16), _r(gu[:, ffn:], torch.bfloat16)
+    ref = _r(g / (1 + torch.exp(-g)) * u, torch.bfloat16)
+    h = x.clone()
+    part = torch.empty(hid // 16, rows, dtype=torch.float32, device=dev)
+    vlasr.decode_linear(m, w_d, epilogue="residual", out=h, ssq_out=part)
+    h_ref = _r(x.float() + _r(m.float() @ w_d.float().t(), torch.bfloat16), torch.bfloat16)
+    torch.cuda.synchronize()
+    assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]
+    assert normwise(to_np(h), to_np(h_ref)) <= TOL["bf16"]
+    hs = h.float().view(rows, hid // 16, 16)
+    assert torch.allclose(part, (hs * hs).sum(-1).t(), rtol=1e-5, atol=1e-5)
+
+
+def test_zz_no_bounded_wait_expired(dev):
+    """Every wait of the tensor-core kernel in this file completed in time."""
+    import ctypes
+    lib = vlasr.load()
+    count = ctypes.c_uint32(12345)
+    assert lib.vl_decode_linear_timeouts(ctypes.byref(count)) == 0
+    assert count.value == 0

@@ -600,6 +600,14 @@ int vl_decode_attention(const void* q, const void* k, const void* v, void* k_cac
       op);
 }
 
+int vl_decode_linear_timeouts(uint32_t* count) {
+  if (count == nullptr) return fail(VL_ERR_INVALID, "vl_decode_linear_timeouts: null pointer");
+  unsigned int v = 0;
+  const cudaError_t err = vl::read_linear_timeouts(&v);
+  if (err == cudaSuccess) *count = v;
+  return exec_status(err, "vl_decode_linear_timeouts");
+}
+
 int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weight,
                      const float* ssq_in, int ssq_in_parts, float eps, const void* w, int64_t n,
                      int64_t k, void* y, int64_t y_row_stride, float* ssq_out, int64_t rows,

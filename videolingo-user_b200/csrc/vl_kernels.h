@@ -117,6 +117,13 @@ struct LinearArgs {
 };
 cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, bool pdl,
                                  cudaStream_t stream);
+// The tensor-core (tcgen05 / TMA / TMEM) form of the same op (vl_linear_tc.cu),
+// used by launch_decode_linear for the shapes it supports.
+bool decode_linear_tc_supported(const LinearArgs& args, int dtype);
+cudaError_t launch_decode_linear_tc(const LinearArgs& args, int dtype, bool pdl,
+                                    cudaStream_t stream);
+// Bounded-wait expiries of the tensor-core kernel on the current device.
+cudaError_t read_linear_timeouts(unsigned int* count);
 
 // Decode-step tail: argmax with the EOS freeze (vl_argmax.cu).
 struct ArgmaxArgs {

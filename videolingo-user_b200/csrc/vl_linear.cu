@@ -391,6 +391,9 @@ cudaError_t linear_typed(const LinearArgs& a, bool pdl, cudaStream_t stream) {
 
 cudaError_t launch_decode_linear(const LinearArgs& a, int dtype, bool pdl, cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;
+  // Output columns in tiles of 128 and k in tiles of 128: the tensor-core
+  // kernel (vl_linear_tc.cu); other shapes: the mma.sync kernel below.
+  if (decode_linear_tc_supported(a, dtype)) return launch_decode_linear_tc(a, dtype, pdl, stream);
   if (dtype == kDtypeBF16) return linear_typed<__nv_bfloat16>(a, pdl, stream);
   if (dtype == kDtypeF16) return linear_typed<__half>(a, pdl, stream);
   return cudaErrorInvalidValue;

@@ -1,0 +1,615 @@
+// Decode-step linear layers on the Blackwell tensor cores (tcgen05 + TMA +
+// TMEM), for sm_100a: y = x W^T for a few token rows (<= 64) against a large
+// weight matrix, with the same fused prologue and epilogues as vl_linear.cu.
+//
+// Reference semantics (VideoLingo-user native/asr/src/decoder.cu, the
+// per-layer decode sequence at :1692-1760): rmsnorm_kernel (:81-101), the
+// cuBLAS projections (`gemm`, :1002-1033, outputs rounded to the storage
+// type), residual_add_kernel (:933-938) and silu_mul_kernel (:103-109).
+//
+// Shape of the problem: the weights stream once from HBM and every weight
+// is used by only a handful of token rows, so the kernel is a weight stream
+// with a tiny matrix product attached.  Design ("swap AB"):
+//   * the 128 output columns of a CTA are the MMA's M = 128 (the weight rows,
+//     operand A) and the token rows, padded to 16 / 32 / 64, are its N
+//     (operand B) - so a 16-row decode step still fills the M=128 tile;
+//   * K is split over a thread-block cluster of S CTAs (S <= 8) so that the
+//     small weight matrices of a decode step still spread over ~150 SMs; the
+//     S partial accumulators are summed through distributed shared memory,
+//     each CTA of the cluster finishing NR / S of the token rows, in a fixed
+//     order (deterministic);
+//   * one thread streams the CTA's weight tiles (128 rows x 64 k, 128-byte
+//     swizzle) with TMA into a ring of up to 6 stages guarded by mbarriers -
+//     for most decode projections the whole K slice is in flight at once,
+//     issued before the programmatic-dependent-launch wait because weights
+//     never depend on the previous kernel;
+//   * the CTA's slice of x (and, with the RMSNorm prologue, x normalised by
+//     the producer's partial sums of squares and the norm weight) is written
+//     by all threads into shared memory in the same swizzled K-major layout;
+//   * one thread issues tcgen05.mma (kind::f16, fp32 accumulate in TMEM);
+//     tcgen05.commit frees ring stages and signals the end;
+//   * the four warps read the accumulator back with tcgen05.ld (warp w owns
+//     TMEM lanes 32w..32w+31 = output columns) for the cluster reduction and
+//     the epilogue: STORE, SWIGLU (gate and up tiles accumulate side by side)
+//     or RESIDUAL (h += y in place, plus the per-16-column sums of squares
+//     the next RMSNorm prologue consumes, in the same format as vl_linear.cu).
+// Every mbarrier wait is bounded: on expiry the CTA stops issuing, waits (also
+// bounded) for its own copies, still meets its cluster barriers, frees its
+// TMEM, writes NaN for its outputs and counts the event in a device word
+// (vl_decode_linear_timeouts()).  No TMA load here uses cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "vl_common.cuh"
+#include "vl_kernels.h"
+
+namespace vl {
+
+// Bounded-wait expiries of the tensor-core decode linear, per device.
+__device__ unsigned int g_linear_wait_timeouts;
+
+namespace {
+
+constexpr int kTcThreads = 128;
+constexpr int kTileM = 128;                 // output columns per CTA (MMA M)
+constexpr int kTileK = 64;                  // k per stage: 64 x 2 B = one 128-byte swizzle row
+constexpr int kTileBytes = kTileM * kTileK * 2;  // 16 KB per weight tile
+constexpr int kMaxStages = 6;
+constexpr size_t kSmemBudget = 220 * 1024;
+constexpr uint32_t kWaitLimit = 1u << 22;   // try_wait polls before a wait gives up (~seconds)
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase with the given parity to complete; false if the bound ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
+// layout: 8-row groups 1024 bytes apart (stride byte offset), version 1,
+// layout type 2 (SWIZZLE_128B).  The k-th 16-element step inside the
+// 128-byte row is the same descriptor with the start address + 32 k bytes.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3fff);          // start address
+  d |= static_cast<uint64_t>(1) << 16;                          // leading byte offset (unused)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                  // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                          // version (sm100)
+  d |= static_cast<uint64_t>(2) << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation, both operands
+// K-major, M = 128, N = n.
+template <typename T>
+__host__ __device__ constexpr uint32_t mma_idesc(int n) {
+  return (1u << 4)                                            // D format F32
+         | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7)   // A format
+         | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10)  // B format
+         | (static_cast<uint32_t>(n >> 3) << 17)              // N >> 3
+         | (static_cast<uint32_t>(kTileM >> 4) << 24);        // M >> 4
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   su32(bar))
+               : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(su32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float2 tc_unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 tc_unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(bf16_lo(w), bf16_hi(w));
+}
+template <>
+__device__ __forceinline__ float2 tc_unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t tc_pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t tc_pack2<__nv_bfloat16>(float lo, float hi) {
+  return pack_bf16x2(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t tc_pack2<__half>(float lo, float hi) {
+  return pack_f16x2(lo, hi);
+}
+
+struct TcLayout {
+  int stages;
+  int chunks;        // k tiles of this CTA
+  size_t ring;       // bytes
+  size_t xs;         // bytes of the x slice
+  size_t part;       // bytes of the partial accumulators
+  size_t total;      // dynamic shared memory (incl. 1 KB alignment slack)
+};
+
+__host__ __device__ inline TcLayout tc_layout(int nr, int epi, int64_t k, int splits,
+                                              int max_stages) {
+  TcLayout L{};
+  L.chunks = static_cast<int>(k / kTileK / splits);
+  const int tiles = epi == VL_LINEAR_SWIGLU ? 2 : 1;
+  L.xs = static_cast<size_t>(nr) * 128 * L.chunks;
+  L.part = static_cast<size_t>(tiles) * nr * kTileM * 4;
+  L.stages = L.chunks < max_stages ? L.chunks : max_stages;
+  while (L.stages > 1 &&
+         static_cast<size_t>(L.stages) * tiles * kTileBytes + L.xs + L.part + 2048 > kSmemBudget)
+    --L.stages;
+  L.ring = static_cast<size_t>(L.stages) * tiles * kTileBytes;
+  L.total = L.ring + L.xs + L.part + 1024 /*align*/ + 1024 /*barriers, tmem slot, inv*/;
+  return L;
+}
+
+template <typename T, int NR, int EPI, bool NORM>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    decode_linear_tc_kernel(const __grid_constant__ LinearArgs a,
+                            const __grid_constant__ CUtensorMap wmap, int splits, int max_stages) {
+  using S = Storage<T>;
+  constexpr int kTiles = EPI == VL_LINEAR_SWIGLU ? 2 : 1;
+  constexpr int kAccCols = kTiles * NR;
+  constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : 128);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, max_stages);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* ring = base;
+  unsigned char* xs = ring + L.ring;
+  float* part = reinterpret_cast<float*>(xs + L.xs);  // [kTiles][NR][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(part) + L.part);
+  uint64_t* full = bars;                    // [stages]
+  uint64_t* empty = bars + kMaxStages;      // [stages]
+  uint64_t* done = bars + 2 * kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 1);
+  int* bad = reinterpret_cast<int*>(tmem_slot + 1);
+  int* issued_s = reinterpret_cast<int*>(tmem_slot + 2);
+  float* inv_s = reinterpret_cast<float*>(tmem_slot + 3);  // [64]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * kTileM;
+  const uint32_t rank = splits > 1 ? cluster_rank() : 0u;
+  const int64_t kbase = static_cast<int64_t>(rank) * L.chunks * kTileK;
+  const int64_t up_row = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < L.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *bad = 0;
+    *issued_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Weight tiles of the first stages: issued before the dependency wait.
+  auto issue = [&](int c) {
+    const int s = c % L.stages;
+    unsigned char* dst = ring + static_cast<size_t>(s) * kTiles * kTileBytes;
+    mbar_expect_tx(&full[s], kTiles * kTileBytes);
+    const int kx = static_cast<int>(kbase + static_cast<int64_t>(c) * kTileK);
+    tma_load_2d(dst, &wmap, kx, static_cast<int>(col0), &full[s]);
+    if (EPI == VL_LINEAR_SWIGLU)
+      tma_load_2d(dst + kTileBytes, &wmap, kx, static_cast<int>(up_row + col0), &full[s]);
+  };
+  int issued = 0;  // producer (thread 0): weight tiles requested so far
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    for (; issued < L.stages; ++issued) issue(issued);
+  }
+  pdl_wait();
+  pdl_release();
+
+  // RMSNorm prologue: 1 / rms of every row from the producer's partial sums
+  // (a warp per row, lane l sums parts l, l+32, ... in order, then a fixed
+  // xor tree), the same order as vl_linear.cu.
+  if (NORM) {
+    for (int r = warp; r < a.rows; r += kTcThreads / 32) {
+      float ssq = 0.0f;
+      for (int p = lane; p < a.ssq_in_parts; p += 32)
+        ssq += a.ssq_in[static_cast<int64_t>(p) * a.rows + r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+      if (lane == 0) inv_s[r] = rsqrtf(ssq / static_cast<float>(a.k) + a.eps);
+    }
+    __syncthreads();
+  }
+
+  // This CTA's x slice into shared memory: k tile c, row r, 16-byte vector v
+  // at c * NR * 128 + r * 128 + ((v ^ (r & 7)) * 16) - the 128-byte swizzle
+  // TMA writes for the weight tiles.  Rows past a.rows are zero.
+  {
+    const T* x = static_cast<const T*>(a.x);
+    const T* gam = static_cast<const T*>(a.norm_weight);
+    const int nvec = NR * L.chunks * 8;
+    for (int i = tid; i < nvec; i += kTcThreads) {
+      const int v = i & 7, r = (i >> 3) % NR, c = (i >> 3) / NR;
+      const int64_t kk = kbase + static_cast<int64_t>(c) * kTileK + v * 8;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (r < a.rows) {
+        val = ld_vec(x + r * a.x_row_stride + kk);
+        if (NORM) {
+          const uint4 g = __ldg(reinterpret_cast<const uint4*>(gam + kk));
+          const float iv = inv_s[r];
+          uint32_t w[4] = {val.x, val.y, val.z, val.w};
+          const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 xv = tc_unpack2<T>(w[j]), gv = tc_unpack2<T>(gw[j]);
+            w[j] = tc_pack2<T>(xv.x * iv * gv.x, xv.y * iv * gv.y);
+          }
+          val = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      *reinterpret_cast<uint4*>(xs + static_cast<size_t>(c) * NR * 128 + r * 128 +
+                                ((v ^ (r & 7)) << 4)) = val;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+
+  constexpr uint32_t kIdesc = mma_idesc<T>(NR);
+  if (tid == 32) {
+    // MMA issuer: 4 k-steps of 16 per stage, fp32 accumulation in TMEM.
+    for (int c = 0; c < L.chunks; ++c) {
+      const int s = c % L.stages;
+      if (!mbar_wait(&full[s], static_cast<uint32_t>((c / L.stages) & 1))) {
+        atomicExch(bad, 1);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a0 = su32(ring + static_cast<size_t>(s) * kTiles * kTileBytes);
+      const uint32_t b0 = su32(xs + static_cast<size_t>(c) * NR * 128);
+#pragma unroll
+      for (int kk = 0; kk < kTileK / 16; ++kk) {
+        const uint64_t bdesc = sw128_desc(b0 + kk * 32);
+        const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
+        mma_f16(tmem, sw128_desc(a0 + kk * 32), bdesc, kIdesc, acc);
+        if (EPI == VL_LINEAR_SWIGLU)
+          mma_f16(tmem + NR, sw128_desc(a0 + kTileBytes + kk * 32), bdesc, kIdesc, acc);
+      }
+      mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    mma_commit(done);
+  } else if (tid == 0) {
+    // Producer: refill each stage once the MMAs of its previous tile are done.
+    for (int c = L.stages; c < L.chunks; ++c) {
+      const int s = c % L.stages;
+      if (*reinterpret_cast<volatile int*>(bad) ||
+          !mbar_wait(&empty[s], static_cast<uint32_t>(((c / L.stages) - 1) & 1))) {
+        atomicExch(bad, 1);
+        break;
+      }
+      issue(c);
+      issued = c + 1;
+    }
+    *issued_s = issued;
+  }
+
+  // Accumulators: warp w holds TMEM lanes (= output columns) 32w..32w+31.
+  const bool finished = mbar_wait(done, 0);
+  __syncwarp();
+  tc_fence_after();
+  float acc[kTiles][NR];
+#pragma unroll
+  for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+    for (int j0 = 0; j0 < NR; j0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + t * NR + j0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[t][j0 + i] = v[i];
+    }
+  tmem_ld_wait();
+  if (!finished) atomicExch(bad, 1);
+#pragma unroll
+  for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+    for (int j = 0; j < NR; ++j) part[(t * NR + j) * kTileM + tid] = acc[t][j];
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  if (*reinterpret_cast<volatile int*>(bad) && tid == 0) {
+    // Error path: let this CTA's copies still in flight land before its
+    // shared memory goes away (bounded): the last tile issued into each
+    // stage, whose phase is the latest one; then count the event.
+    const int n = *issued_s;
+    for (int c = n - L.stages < 0 ? 0 : n - L.stages; c < n; ++c)
+      (void)mbar_wait(&full[c % L.stages], static_cast<uint32_t>((c / L.stages) & 1));
+    atomicAdd(&g_linear_wait_timeouts, 1u);
+  }
+
+  // Sum the cluster's partials for this CTA's NR / splits token rows, in
+  // rank order, and finish them.
+  if (splits > 1) cluster_sync();
+  const int rp = NR / splits;
+  const int r_begin = static_cast<int>(rank) * rp;
+  T* y = static_cast<T*>(a.y);
+  float* hbuf = part;  // RESIDUAL: this CTA's new h values, [rp][128], after a barrier
+  float hv_keep[NR];
+#pragma unroll
+  for (int jj = 0; jj < NR; ++jj) {
+    if (jj >= rp) break;
+    const int j = r_begin + jj;
+    float v[kTiles];
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) {
+      float s = 0.0f;
+      for (int p = 0; p < splits; ++p) {
+        const float* src = part + (t * NR + j) * kTileM + tid;
+        s += splits > 1 ? ld_cluster_f32(src, static_cast<uint32_t>(p)) : *src;
+      }
+      v[t] = s;
+    }
+    hv_keep[jj] = 0.0f;
+    if (j >= a.rows) continue;
+    T* dst = y + j * a.y_row_stride + col0 + tid;
+    const bool ok = !*reinterpret_cast<volatile int*>(bad);
+    if (EPI == VL_LINEAR_STORE) {
+      *dst = S::from_float(ok ? v[0] : __int_as_float(0x7fc00000));
+    } else if (EPI == VL_LINEAR_SWIGLU) {
+      const float g = S::round_trip(v[0]);
+      const float u = S::round_trip(v[kTiles - 1]);
+      *dst = S::from_float(ok ? __fdividef(g, 1.0f + __expf(-g)) * u : __int_as_float(0x7fc00000));
+    } else {
+      const float hv = S::round_trip(S::to_float(*dst) + S::round_trip(v[0]));
+      *dst = S::from_float(ok ? hv : __int_as_float(0x7fc00000));
+      hv_keep[jj] = hv;
+    }
+  }
+  if (splits > 1) cluster_sync();  // every CTA is done reading the others' partials
+  if (EPI == VL_LINEAR_RESIDUAL && a.ssq_out != nullptr) {
+    __syncthreads();
+#pragma unroll
+    for (int jj = 0; jj < NR; ++jj)
+      if (jj < rp) hbuf[jj * kTileM + tid] = hv_keep[jj];
+    __syncthreads();
+    // per row and 16-column group, sum of squares in column order (fmaf),
+    // as vl_linear.cu writes it: ssq_out[col / 16][row]
+    for (int i = tid; i < rp * (kTileM / 16); i += kTcThreads) {
+      const int jj = i / (kTileM / 16), g = i % (kTileM / 16);
+      const int j = r_begin + jj;
+      if (j >= a.rows) continue;
+      float ssq = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) ssq = fmaf(hbuf[jj * kTileM + g * 16 + c],
+                                              hbuf[jj * kTileM + g * 16 + c], ssq);
+      a.ssq_out[(col0 / 16 + g) * a.rows + j] = ssq;
+    }
+  }
+}
+
+using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeTiled encode_fn() {
+  static std::atomic<EncodeTiled> fn{nullptr};
+  EncodeTiled f = fn.load(std::memory_order_acquire);
+  if (f != nullptr) return f;
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || p == nullptr) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  f = reinterpret_cast<EncodeTiled>(p);
+  fn.store(f, std::memory_order_release);
+  return f;
+}
+
+// K splits: the fewest (a power of two, at most 8, dividing the k tiles) that
+// give at least one CTA per SM, keeping at least 2 k tiles per CTA.
+int tc_splits(int64_t tiles, int64_t ktiles, int nr) {
+  const int64_t want = sm_count();
+  int s = 1;
+  while (s < 8 && tiles * s < want && ktiles % (2 * s) == 0 && ktiles / (2 * s) >= 2 &&
+         nr / (2 * s) >= 1)
+    s *= 2;
+  return s;
+}
+
+template <typename T, int NR, int EPI, bool NORM>
+cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cudaStream_t stream) {
+  const int64_t cols = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
+  const int64_t tiles = cols / kTileM;
+  const int splits = tc_splits(tiles, a.k / kTileK, NR);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, kMaxStages);
+  auto kernel = decode_linear_tc_kernel<T, NR, EPI, NORM>;
+  static std::atomic<size_t> configured[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || configured[dev].load(std::memory_order_acquire) < L.total) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBudget + 2048));
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev].store(kSmemBudget + 2048, std::memory_order_release);
+  }
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = 1;
+  attr[na].val.clusterDim.y = static_cast<unsigned>(splits);
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(splits), 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, a, map, splits, static_cast<int>(kMaxStages));
+}
+
+template <typename T, int NR>
+cudaError_t tc_epi(const LinearArgs& a, const CUtensorMap& map, bool pdl, cudaStream_t stream) {
+  const bool norm = a.norm_weight != nullptr;
+  switch (a.epilogue) {
+    case VL_LINEAR_STORE:
+      return norm ? tc_launch<T, NR, VL_LINEAR_STORE, true>(a, map, pdl, stream)
+                  : tc_launch<T, NR, VL_LINEAR_STORE, false>(a, map, pdl, stream);
+    case VL_LINEAR_SWIGLU:
+      return norm ? tc_launch<T, NR, VL_LINEAR_SWIGLU, true>(a, map, pdl, stream)
+                  : tc_launch<T, NR, VL_LINEAR_SWIGLU, false>(a, map, pdl, stream);
+    default:
+      return norm ? tc_launch<T, NR, VL_LINEAR_RESIDUAL, true>(a, map, pdl, stream)
+                  : tc_launch<T, NR, VL_LINEAR_RESIDUAL, false>(a, map, pdl, stream);
+  }
+}
+
+template <typename T>
+cudaError_t tc_typed(const LinearArgs& a, const CUtensorMap& map, bool pdl, cudaStream_t stream) {
+  if (a.rows <= 16) return tc_epi<T, 16>(a, map, pdl, stream);
+  if (a.rows <= 32) return tc_epi<T, 32>(a, map, pdl, stream);
+  return tc_epi<T, 64>(a, map, pdl, stream);
+}
+
+}  // namespace
+
+cudaError_t read_linear_timeouts(unsigned int* count) {
+  return cudaMemcpyFromSymbol(count, g_linear_wait_timeouts, sizeof(unsigned int));
+}
+
+bool decode_linear_tc_supported(const LinearArgs& a, int dtype) {
+  if (dtype != kDtypeBF16 && dtype != kDtypeF16) return false;
+  const int64_t cols = a.epilogue == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
+  if (a.rows < 1 || a.rows > 64 || cols % kTileM != 0 || a.k % (2 * kTileK) != 0) return false;
+  if (a.n > (int64_t(1) << 31) - 1 || a.k > (int64_t(1) << 31) - 1) return false;
+  if (!aligned16(a.w) || !aligned16(a.x) || a.x_row_stride % 8 != 0) return false;
+  if (a.norm_weight != nullptr && !aligned16(a.norm_weight)) return false;
+  const int nr = a.rows <= 16 ? 16 : (a.rows <= 32 ? 32 : 64);
+  const int splits = tc_splits(cols / kTileM, a.k / kTileK, nr);
+  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, kMaxStages);
+  if (L.stages < 1 || L.total > kSmemBudget + 2048) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t launch_decode_linear_tc(const LinearArgs& a, int dtype, bool pdl,
+                                    cudaStream_t stream) {
+  EncodeTiled encode = encode_fn();
+  if (encode == nullptr) return cudaErrorNotSupported;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.k), static_cast<cuuint64_t>(a.n)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.k) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), static_cast<cuuint32_t>(kTileM)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(&map,
+                            dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            2, const_cast<void*>(a.w), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (dtype == kDtypeBF16) return tc_typed<__nv_bfloat16>(a, map, pdl, stream);
+  return tc_typed<__half>(a, map, pdl, stream);
+}
+
+}  // namespace vl

@@ -60,6 +60,7 @@ SIGNATURES = {
     "vl_decode_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
                                  c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int,
                                  c_int, c_int, c_void_p]),
+    "vl_decode_linear_timeouts": (c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "vl_argmax_eos": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                               c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                               ctypes.POINTER(c_int64), c_int, c_int64, c_int, c_void_p,

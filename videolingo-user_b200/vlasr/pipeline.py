@@ -356,38 +356,57 @@ class EncoderNormChain:
 
     # -- host-buffer path -----------------------------------------------------
     def step_host(self, pcm_host: torch.Tensor, mel_host: torch.Tensor, y_host: torch.Tensor,
-                  pcm_dev: torch.Tensor, groups: int = 4) -> None:
+                  pcm_dev: torch.Tensor, groups: int = 4, trace: list | None = None) -> None:
         """Host PCM [chunks, 480000] -> host mel [chunks,128,3000] and host
         encoder-norm outputs [chunks*frames, hidden] (pinned buffers).
 
         Chunk groups flow through three streams: group g+1's PCM uploads while
-        group g computes and group g-1's results download."""
+        group g computes and group g-1's results download.  With `trace` (a
+        list), (kind, start, end) CUDA event pairs are appended for every
+        upload ("h2d"), group computation ("compute") and download ("d2h")."""
         s = self.shape
         cur = torch.cuda.current_stream(self.device)
         up = torch.cuda.Stream(self.device)
         down = torch.cuda.Stream(self.device)
         bounds = host_group_bounds(s.chunks, groups)
+
+        def mark(stream):
+            if trace is None:
+                return None
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            return ev
+
         self._begin_step()
         uploaded = []
         up.wait_stream(cur)
         with torch.cuda.stream(up):
             for c0, c1 in bounds:
+                a = mark(up)
                 pcm_dev[c0:c1].copy_(pcm_host[c0:c1], non_blocking=True)
-                ev = torch.cuda.Event()
+                ev = torch.cuda.Event(enable_timing=trace is not None)
                 ev.record(up)
                 uploaded.append(ev)
+                if trace is not None:
+                    trace.append(("h2d", a, ev))
         for (c0, c1), ev in zip(bounds, uploaded):
             cur.wait_event(ev)
+            a = mark(cur)
             self.run_mel(pcm_dev, c0, c1)
             r0, r1 = c0 * s.frames, c1 * s.frames
             for l in range(s.layers):
                 self.run_layer(l, r0, r1)
-            done = torch.cuda.Event()
+            done = torch.cuda.Event(enable_timing=trace is not None)
             done.record(cur)
+            if trace is not None:
+                trace.append(("compute", a, done))
             down.wait_event(done)
             with torch.cuda.stream(down):
+                a = mark(down)
                 mel_host[c0:c1].copy_(self.mel[c0:c1], non_blocking=True)
                 y_host[r0:r1].copy_(self.y[r0:r1], non_blocking=True)
+                if trace is not None:
+                    trace.append(("d2h", a, mark(down)))
         cur.wait_stream(down)
         self._end_step()
 
