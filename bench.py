@@ -63,6 +63,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--chunks", type=int, default=TOTAL_CHUNKS)
     p.add_argument("--no-ops", action="store_true", help="skip the per-op roofline table")
+    p.add_argument("--ops", action="store_true",
+                   help="with --impl reference: time the reference's own GPU layer kernels "
+                        "(oracle/_ref) at the op table's shapes")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--nccl-channels", type=int, default=None,
@@ -525,10 +528,165 @@ def cpu_baseline(target_s: float = 12.0) -> dict:
             "seconds": round(res["total_s"], 2)}
 
 
+def reference_gpu_ops(peak: float) -> dict:
+    """The reference's own FP16 layer kernels (native/asr/src/engine.cu and
+    decoder.cu, compiled from its sources into oracle/_ref/libvlref.so) on this
+    GPU at the op table's shapes, with the same timing (L2 flushed before every
+    launch, CUDA events, launches queued behind a device spin).  Where the
+    reference runs a sequence for one of this library's fused ops, the whole
+    sequence is timed (residual add + copy + norm).  Its compile-time shapes
+    apply: decoder RoPE rotates all 128 dims from 1024-position tables, its
+    embedding table has 59264 rows.  compute_mel_batched is its host-to-host
+    entry point and is timed by the host clock."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import oracle
+    lib = oracle.load_reference_kernels()
+    if lib is None:
+        return {"unavailable": "oracle/_ref/libvlref.so not built"}
+    P, I, U = ctypes.c_void_p, ctypes.c_int, ctypes.c_ulonglong
+    sig = {"vlref_layer_norm": [P, P, P, I, I], "vlref_residual_add_enc": [P, P, U],
+           "vlref_gelu": [P, U], "vlref_rmsnorm": [P, P, I, I],
+           "vlref_residual_add_dec": [P, P, U], "vlref_silu_mul": [P, P, U],
+           "vlref_fill_rope_tables": [P, P], "vlref_rope_rows_t": [P, P, P, P, I, I],
+           "vlref_rope_map_t": [P, P, P, P, P, P, I],
+           "vlref_gather_batch": [ctypes.c_void_p, I, P, P, I, P, I],
+           "vlref_append_kv_mapped": [P, P, P, P, P, P, I, U],
+           "vlref_compute_mel_batched": [P, I, P]}
+    for name, args in sig.items():
+        getattr(lib, name).argtypes = args
+        getattr(lib, name).restype = I
+    dev = torch.device("cuda")
+    h = torch.float16
+    g = torch.Generator(device=dev).manual_seed(4321)
+    flush_buf = torch.ones(128 * 1024 * 1024, dtype=torch.int32, device=dev)
+    flush = lambda: flush_buf.max()  # noqa: E731
+
+    def rnd(shape, mean=0.0, std=1.0):
+        t = torch.empty(shape, device=dev, dtype=torch.float32)
+        t.normal_(mean, std, generator=g)
+        return t.to(h)
+
+    def ptr(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def chk(rc):
+        if rc != 0:
+            raise RuntimeError(f"reference kernel launch failed ({rc})")
+
+    rows = {}
+
+    def run(name, config, nbytes, fn, latency=False, iters=20):
+        fn()
+        torch.cuda.synchronize()
+        ms = time_op(fn, iters, flush)
+        e = {"config": config, "bytes": nbytes, "us": round(ms * 1e3, 2)}
+        if not latency:
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            e.update({"gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 3)})
+        rows[name] = e
+
+    def add_norm_seq(x, d, ln, launch):
+        def fn():
+            chk(lib.vlref_residual_add_enc(ptr(x), ptr(d), x.numel()) if launch == "ln" else
+                lib.vlref_residual_add_dec(ptr(x), ptr(d), x.numel()))
+            ln.copy_(x)
+        return fn
+
+    x, d, ln = rnd((12000, 1280)), rnd((12000, 1280)), torch.empty(12000, 1280, dtype=h, device=dev)
+    gam, bet = rnd(1280, 1.0, 0.02), rnd(1280, 0.0, 0.02)
+    seq = add_norm_seq(x, d, ln, "ln")
+    run("add_layernorm", "[8,1500,1280] fp16: residual_add_kernel + cudaMemcpy + layer_norm_kernel",
+        4 * x.numel() * 2,
+        lambda: (seq(), chk(lib.vlref_layer_norm(ptr(ln), ptr(gam), ptr(bet), 12000, 1280))))
+    del x, d, ln
+    gi = rnd((12000, 5120))
+    run("gelu_erf", "[8,1500,5120] fp16 gelu_kernel (in place)", 2 * gi.numel() * 2,
+        lambda: chk(lib.vlref_gelu(ptr(gi), gi.numel())))
+    del gi
+    x, d, ln = rnd((8192, 2048)), rnd((8192, 2048)), torch.empty(8192, 2048, dtype=h, device=dev)
+    w = rnd(2048, 1.0, 0.02)
+    seq = add_norm_seq(x, d, ln, "rms")
+    run("add_rmsnorm", "[4,2048,2048] fp16: residual_add_kernel + cudaMemcpy + rmsnorm_kernel",
+        4 * x.numel() * 2,
+        lambda: (seq(), chk(lib.vlref_rmsnorm(ptr(ln), ptr(w), 8192, 2048))))
+    del x, d, ln
+    gt, up = rnd((8192, 6144)), rnd((8192, 6144))
+    run("swiglu", "gate/up [4,2048,6144] fp16 silu_mul_kernel (into gate)", 3 * gt.numel() * 2,
+        lambda: chk(lib.vlref_silu_mul(ptr(gt), ptr(up), gt.numel())))
+    del gt, up
+    cos_t = torch.empty(1024 * 64, dtype=torch.float32, device=dev)
+    sin_t = torch.empty_like(cos_t)
+    chk(lib.vlref_fill_rope_tables(ptr(cos_t), ptr(sin_t)))
+    q, k = rnd((8192, 2048)), rnd((8192, 512))
+    run("rope", "Q [4,2048,16,128] K [4,2048,4,128] fp16 rope_rows_kernel, rotary 128 "
+        "(its compile-time shape), positions row % 1024 (its table size)",
+        (q.numel() + k.numel()) * 2 * 2,
+        lambda: chk(lib.vlref_rope_rows_t(ptr(q), ptr(k), ptr(cos_t), ptr(sin_t), 8192, 1024)))
+    del q, k
+    table = rnd((59264, 2048), 0.0, 0.02)
+    ids = torch.randint(0, 59264, (2048,), device=dev, generator=g, dtype=torch.int64)
+    eo = torch.empty(4, 2048, 2048, dtype=h, device=dev)
+    run("embed_gather", "ids [2048] x 4 chunks from [59264,2048] fp16 gather_batch_kernel",
+        2 * eo.numel() * 2 + 4 * ids.numel() * 8,
+        lambda: chk(lib.vlref_gather_batch(ptr(ids), 2048, ptr(table), ptr(table), 0, ptr(eo), 4)))
+    del table, eo
+    x, d, ln = rnd((64, 2048)), rnd((64, 2048)), torch.empty(64, 2048, dtype=h, device=dev)
+    seq = add_norm_seq(x, d, ln, "rms")
+    run("decode_add_rmsnorm", "[64,2048] fp16: residual_add_kernel + cudaMemcpy + rmsnorm_kernel",
+        4 * x.numel() * 2, lambda: (seq(), chk(lib.vlref_rmsnorm(ptr(ln), ptr(w), 64, 2048))),
+        latency=True)
+    q, k, v = rnd((64, 2048)), rnd((64, 512)), rnd((64, 512))
+    pos = torch.randint(0, 1024, (64,), device=dev, generator=g, dtype=torch.int32)
+    act = torch.arange(64, device=dev, dtype=torch.int32)
+    run("decode_rope", "Q [64,16,128] K [64,4,128] fp16 rope_at_position_map_kernel, rotary 128",
+        (q.numel() + k.numel()) * 2 * 2,
+        lambda: chk(lib.vlref_rope_map_t(ptr(q), ptr(k), ptr(cos_t), ptr(sin_t), ptr(pos), ptr(act),
+                                         64)), latency=True)
+    kc = torch.zeros(64 * 1024, 512, dtype=h, device=dev)
+    vc = torch.zeros_like(kc)
+    run("decode_kv_append", "K/V [64,4,128] fp16 append_kv_mapped_kernel, 64 chunks x 1024 slots",
+        4 * k.numel() * 2,
+        lambda: chk(lib.vlref_append_kv_mapped(ptr(k), ptr(v), ptr(kc), ptr(vc), ptr(pos), ptr(act),
+                                               64, 1024 * 512)), latency=True)
+    del kc, vc, flush_buf
+    torch.cuda.empty_cache()
+    from vlasr.synth import audio_chunks
+    for chunks in (32, 1):
+        pcm = np.ascontiguousarray(audio_chunks(chunks, seed=7), np.float32)
+        out = np.empty((chunks, 128, 3000), np.float32)
+        fn = lambda: chk(lib.vlref_compute_mel_batched(pcm.ctypes.data, chunks,  # noqa: E731
+                                                       out.ctypes.data))
+        fn()
+        reps = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            fn()
+            reps.append(time.perf_counter() - t0)
+        sec = min(reps)
+        rows[f"logmel_{chunks}chunk" + ("s" if chunks > 1 else "")] = {
+            "config": f"{chunks} x 30 s chunks, compute_mel_batched (host in / host out: mallocs, "
+                      "H2D, five kernels, D2H; best of 3 by the host clock)",
+            "bytes": chunks * 3456000, "us": round(sec * 1e6, 1),
+            "audio_s_per_s": round(chunks * AUDIO_SECONDS_PER_CHUNK / sec, 1)}
+    return rows
+
+
 def run_reference_arm(args) -> None:
-    """`--impl reference`: the reference's CPU path on this box (rank 0 only)."""
+    """`--impl reference`: the reference's CPU path on this box (rank 0 only);
+    with --ops, the reference's own GPU layer kernels at the op table's shapes."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.ops:
+        import torch
+        torch.cuda.set_device(0)
+        peak, _ = peaks()
+        print(json.dumps({"impl": "reference", "ops_reference_gpu": reference_gpu_ops(peak)}),
+              flush=True)
         return
     from oracle import cpu_reference
     threads = os.cpu_count() or 1
@@ -1091,12 +1249,14 @@ def main() -> None:
     bytes_step = shape.bytes_per_step()
     gelu_us = breakdown["gelu"]["mean_us"]
     gelu_gbs = bytes_step["gelu"] / (gelu_us * 1e-6) / 1e9
+    # DRAM bytes per launch: the ratio dram/algorithmic bytes measured by ncu
+    # on a 4.1 GB GELU launch (profiles/traffic.json) times this launch's bytes
     traffic = None
     tpath = ROOT / "profiles" / "traffic.json"
     if tpath.exists():
         try:
-            per_row = json.loads(tpath.read_text())["gelu_erf"]["dram_bytes_per_row"]
-            traffic = int(per_row * shape.rows)
+            ratio = json.loads(tpath.read_text())["gelu_erf"]["dram_bytes_per_algorithmic_byte"]
+            traffic = int(ratio * bytes_step["gelu"])
         except Exception:  # noqa: BLE001
             traffic = None
     roofline = {"bound": "hbm", "kernel": "gelu_erf (vl_gelu_erf)", "achieved": round(gelu_gbs, 1),

@@ -114,4 +114,29 @@ int vlref_attention_mapped(const void* q, const void* kv_cache, void* out, const
   return static_cast<int>(cudaGetLastError());
 }
 
+// Kernel-only RoPE launchers for timing (bench.py --impl reference --ops):
+// the reference's tables (kMaxSequence x 64 floats each) are built once into
+// caller device buffers, so a timed launch is the kernel alone.
+int vlref_fill_rope_tables(float* cos_dev, float* sin_dev) {
+  const std::vector<float> c = build_full_rope_table(true), s = build_full_rope_table(false);
+  cudaError_t err = cudaMemcpy(cos_dev, c.data(), c.size() * sizeof(float), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess)
+    err = cudaMemcpy(sin_dev, s.data(), s.size() * sizeof(float), cudaMemcpyHostToDevice);
+  return static_cast<int>(err);
+}
+
+int vlref_rope_rows_t(void* q, void* k, const float* cos_dev, const float* sin_dev, int rows,
+                      int frames) {
+  rope_rows_kernel<<<rows, 64>>>(static_cast<half*>(q), static_cast<half*>(k), cos_dev, sin_dev,
+                                 rows, frames);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int vlref_rope_map_t(void* q, void* k, const float* cos_dev, const float* sin_dev,
+                     const int* positions, const int* active, int rows) {
+  rope_at_position_map_kernel<<<rows, 64>>>(static_cast<half*>(q), static_cast<half*>(k), cos_dev,
+                                            sin_dev, positions, active, rows);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // extern "C"

@@ -211,8 +211,10 @@ struct TcLayout {
   size_t total;      // dynamic shared memory (incl. 1 KB alignment slack)
 };
 
+// budget: shared memory one CTA may take (so that the grid's CTAs are
+// resident in one wave, see tc_budget).
 __host__ __device__ inline TcLayout tc_layout(int nr, int epi, int64_t k, int splits,
-                                              int max_stages) {
+                                              int max_stages, size_t budget) {
   TcLayout L{};
   L.chunks = static_cast<int>(k / kTileK / splits);
   const int tiles = epi == VL_LINEAR_SWIGLU ? 2 : 1;
@@ -220,7 +222,7 @@ __host__ __device__ inline TcLayout tc_layout(int nr, int epi, int64_t k, int sp
   L.part = static_cast<size_t>(tiles) * nr * kTileM * 4;
   L.stages = L.chunks < max_stages ? L.chunks : max_stages;
   while (L.stages > 1 &&
-         static_cast<size_t>(L.stages) * tiles * kTileBytes + L.xs + L.part + 2048 > kSmemBudget)
+         static_cast<size_t>(L.stages) * tiles * kTileBytes + L.xs + L.part + 2048 > budget)
     --L.stages;
   L.ring = static_cast<size_t>(L.stages) * tiles * kTileBytes;
   L.total = L.ring + L.xs + L.part + 1024 /*align*/ + 1024 /*barriers, tmem slot, inv*/;
@@ -230,12 +232,13 @@ __host__ __device__ inline TcLayout tc_layout(int nr, int epi, int64_t k, int sp
 template <typename T, int NR, int EPI, bool NORM>
 __global__ void __launch_bounds__(kTcThreads, 1)
     decode_linear_tc_kernel(const __grid_constant__ LinearArgs a,
-                            const __grid_constant__ CUtensorMap wmap, int splits, int max_stages) {
+                            const __grid_constant__ CUtensorMap wmap, int splits, int max_stages,
+                            unsigned int budget) {
   using S = Storage<T>;
   constexpr int kTiles = EPI == VL_LINEAR_SWIGLU ? 2 : 1;
   constexpr int kAccCols = kTiles * NR;
   constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : 128);
-  const TcLayout L = tc_layout(NR, EPI, a.k, splits, max_stages);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, max_stages, budget);
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -347,6 +350,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
 
   constexpr uint32_t kIdesc = mma_idesc<T>(NR);
+  // Roles: lane 0 of warp 1 issues the MMAs, lane 0 of warp 0 refills the
+  // ring; the other lanes of those two warps park at __syncwarp (a spinning
+  // lane in the same warp would hold the issuing lane back).
   if (tid == 32) {
     // MMA issuer: 4 k-steps of 16 per stage, fp32 accumulation in TMEM.
     for (int c = 0; c < L.chunks; ++c) {
@@ -383,6 +389,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     *issued_s = issued;
   }
+  if (warp < 2) __syncwarp();
 
   // Accumulators: warp w holds TMEM lanes (= output columns) 32w..32w+31.
   const bool finished = mbar_wait(done, 0);
@@ -510,12 +517,21 @@ int tc_splits(int64_t tiles, int64_t ktiles, int nr) {
   return s;
 }
 
+// Shared memory per CTA such that every CTA of the grid is resident at once
+// (228 KB per SM shared by ceil(ctas / SMs) CTAs), at most kSmemBudget.
+size_t tc_budget(int64_t ctas) {
+  const int64_t per_sm = (ctas + sm_count() - 1) / sm_count();
+  const size_t fit = per_sm > 1 ? static_cast<size_t>(227 * 1024 / per_sm) - 1024 - 2048 : kSmemBudget;
+  return fit < kSmemBudget ? fit : kSmemBudget;
+}
+
 template <typename T, int NR, int EPI, bool NORM>
 cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cudaStream_t stream) {
   const int64_t cols = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
   const int64_t tiles = cols / kTileM;
   const int splits = tc_splits(tiles, a.k / kTileK, NR);
-  const TcLayout L = tc_layout(NR, EPI, a.k, splits, kMaxStages);
+  const size_t budget = tc_budget(tiles * splits);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, kMaxStages, budget);
   auto kernel = decode_linear_tc_kernel<T, NR, EPI, NORM>;
   static std::atomic<size_t> configured[64];
   int dev = 0;
@@ -546,7 +562,8 @@ cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cud
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kernel, a, map, splits, static_cast<int>(kMaxStages));
+  return cudaLaunchKernelEx(&cfg, kernel, a, map, splits, static_cast<int>(kMaxStages),
+                            static_cast<unsigned int>(budget));
 }
 
 template <typename T, int NR>
@@ -587,7 +604,8 @@ bool decode_linear_tc_supported(const LinearArgs& a, int dtype) {
   if (a.norm_weight != nullptr && !aligned16(a.norm_weight)) return false;
   const int nr = a.rows <= 16 ? 16 : (a.rows <= 32 ? 32 : 64);
   const int splits = tc_splits(cols / kTileM, a.k / kTileK, nr);
-  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, kMaxStages);
+  const size_t budget = tc_budget(cols / kTileM * splits);
+  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, kMaxStages, budget);
   if (L.stages < 1 || L.total > kSmemBudget + 2048) return false;
   return encode_fn() != nullptr;
 }
