@@ -135,41 +135,42 @@ __device__ __forceinline__ c2 cmul_conj(c2 a, float c, float s) {
   return fma2(swap(a), mk(s, -s), mul(a, mk(c, c)));
 }
 
-// In-place forward DFT of 20 complex points: X[k] = sum_n x[n] exp(-2 pi i k n / 20).
-// 20 = 4 x 5: n = 5a + b, k = c + 4d.  DFT-4 over a, twiddle W20^(b c),
-// DFT-5 over b.
+// In-place forward DFT of 20 complex points: X[k] = sum_n x[n] exp(-2 pi i k n / 20),
+// by the prime-factor (Good-Thomas) split 20 = 4 x 5: with gcd(4, 5) = 1,
+// n = (5 n1 + 4 n2) mod 20 and k = (5 k1 + 16 k2) mod 20 turn the DFT-20
+// into DFT-4s over n1 followed by DFT-5s over n2 with no twiddle factors in
+// between (W20^(nk) = W4^(n1 k1) W5^(n2 k2)).  The index maps are fixed,
+// so they cost nothing in unrolled register code.
 __device__ __forceinline__ void dft20(c2 (&x)[20]) {
-  c2 u[5][4];
+  c2 u[5][4];  // u[n2][k1]
 #pragma unroll
-  for (int b = 0; b < 5; ++b) {
-    const c2 t0 = add(x[b], x[10 + b]), t1 = sub(x[b], x[10 + b]);
-    const c2 t2 = add(x[5 + b], x[15 + b]), t3 = sub(x[5 + b], x[15 + b]);
-    u[b][0] = add(t0, t2);
-    u[b][2] = sub(t0, t2);
-    u[b][1] = sub_i(t1, t3);
-    u[b][3] = add_i(t1, t3);
+  for (int n2 = 0; n2 < 5; ++n2) {
+    const c2 a0 = x[(4 * n2) % 20], a1 = x[(5 + 4 * n2) % 20];
+    const c2 a2 = x[(10 + 4 * n2) % 20], a3 = x[(15 + 4 * n2) % 20];
+    const c2 t0 = add(a0, a2), t1 = sub(a0, a2);
+    const c2 t2 = add(a1, a3), t3 = sub(a1, a3);
+    u[n2][0] = add(t0, t2);
+    u[n2][2] = sub(t0, t2);
+    u[n2][1] = sub_i(t1, t3);
+    u[n2][3] = add_i(t1, t3);
   }
-#pragma unroll
-  for (int b = 1; b < 5; ++b)
-#pragma unroll
-    for (int c = 1; c < 4; ++c) u[b][c] = cmul_conj(u[b][c], mel::w20_cos(b * c), mel::w20_sin(b * c));
   const c2 C1 = mk(mel::kC1, mel::kC1), C2 = mk(mel::kC2, mel::kC2);
   const c2 S1 = mk(mel::kS1, mel::kS1), S2 = mk(mel::kS2, mel::kS2);
   const c2 NS1 = mk(-mel::kS1, -mel::kS1);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const c2 x0 = u[0][c];
-    const c2 a1 = add(u[1][c], u[4][c]), a2 = add(u[2][c], u[3][c]);
-    const c2 b1 = sub(u[1][c], u[4][c]), b2 = sub(u[2][c], u[3][c]);
+  for (int k1 = 0; k1 < 4; ++k1) {
+    const c2 x0 = u[0][k1];
+    const c2 a1 = add(u[1][k1], u[4][k1]), a2 = add(u[2][k1], u[3][k1]);
+    const c2 b1 = sub(u[1][k1], u[4][k1]), b2 = sub(u[2][k1], u[3][k1]);
     const c2 m1 = fma2(a2, C2, fma2(a1, C1, x0));
     const c2 m2 = fma2(a2, C1, fma2(a1, C2, x0));
     const c2 n1 = fma2(b2, S2, mul(b1, S1));
     const c2 n2 = fma2(b2, NS1, mul(b1, S2));
-    x[c] = add(x0, add(a1, a2));
-    x[c + 4] = sub_i(m1, n1);
-    x[c + 16] = add_i(m1, n1);
-    x[c + 8] = sub_i(m2, n2);
-    x[c + 12] = add_i(m2, n2);
+    x[(5 * k1) % 20] = add(x0, add(a1, a2));        // k2 = 0
+    x[(5 * k1 + 16) % 20] = sub_i(m1, n1);          // k2 = 1
+    x[(5 * k1 + 4) % 20] = add_i(m1, n1);           // k2 = 4
+    x[(5 * k1 + 12) % 20] = sub_i(m2, n2);          // k2 = 2
+    x[(5 * k1 + 8) % 20] = add_i(m2, n2);           // k2 = 3
   }
 }
 
