@@ -173,12 +173,21 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// A float of CTA `rank`'s shared memory at the address of `local` in this
+// CTA.  Only called between cluster barriers (which order it); no memory
+// clobber, so a run of these loads issues back to back.
 __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(su32(local)), "r"(rank));
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
   return v;
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
 }
 
 template <typename T>
@@ -301,9 +310,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   pdl_wait();
   pdl_release();
 
+  // This CTA's x slice into shared memory with cp.async (rows past a.rows
+  // zero-filled): k tile c, row r, 16-byte vector v at
+  // c * NR * 128 + r * 128 + ((v ^ (r & 7)) * 16) - the 128-byte swizzle TMA
+  // writes for the weight tiles.  In flight while the RMSNorm sums load.
+  const int nvec = NR * L.chunks * 8;
+  {
+    const T* x = static_cast<const T*>(a.x);
+    for (int i = tid; i < nvec; i += kTcThreads) {
+      const int v = i & 7, r = (i >> 3) % NR, c = (i >> 3) / NR;
+      const int64_t kk = kbase + static_cast<int64_t>(c) * kTileK + v * 8;
+      const bool ok = r < a.rows;
+      cp_async16_zfill(xs + static_cast<size_t>(c) * NR * 128 + r * 128 + ((v ^ (r & 7)) << 4),
+                       x + (ok ? r : 0) * a.x_row_stride + kk, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   // RMSNorm prologue: 1 / rms of every row from the producer's partial sums
   // (a warp per row, lane l sums parts l, l+32, ... in order, then a fixed
-  // xor tree), the same order as vl_linear.cu.
+  // xor tree), the same order as vl_linear.cu; then x = round(x * inv * w)
+  // in place in shared memory.
   if (NORM) {
     for (int r = warp; r < a.rows; r += kTcThreads / 32) {
       float ssq = 0.0f;
@@ -313,40 +339,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
       if (lane == 0) inv_s[r] = rsqrtf(ssq / static_cast<float>(a.k) + a.eps);
     }
-    __syncthreads();
   }
-
-  // This CTA's x slice into shared memory: k tile c, row r, 16-byte vector v
-  // at c * NR * 128 + r * 128 + ((v ^ (r & 7)) * 16) - the 128-byte swizzle
-  // TMA writes for the weight tiles.  Rows past a.rows are zero.
-  {
-    const T* x = static_cast<const T*>(a.x);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  if (NORM) {
     const T* gam = static_cast<const T*>(a.norm_weight);
-    const int nvec = NR * L.chunks * 8;
     for (int i = tid; i < nvec; i += kTcThreads) {
       const int v = i & 7, r = (i >> 3) % NR, c = (i >> 3) / NR;
+      if (r >= a.rows) continue;
       const int64_t kk = kbase + static_cast<int64_t>(c) * kTileK + v * 8;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (r < a.rows) {
-        val = ld_vec(x + r * a.x_row_stride + kk);
-        if (NORM) {
-          const uint4 g = __ldg(reinterpret_cast<const uint4*>(gam + kk));
-          const float iv = inv_s[r];
-          uint32_t w[4] = {val.x, val.y, val.z, val.w};
-          const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint4* slot = reinterpret_cast<uint4*>(xs + static_cast<size_t>(c) * NR * 128 + r * 128 +
+                                             ((v ^ (r & 7)) << 4));
+      const uint4 val = *slot;
+      const uint4 g = __ldg(reinterpret_cast<const uint4*>(gam + kk));
+      const float iv = inv_s[r];
+      uint32_t w[4] = {val.x, val.y, val.z, val.w};
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 xv = tc_unpack2<T>(w[j]), gv = tc_unpack2<T>(gw[j]);
-            w[j] = tc_pack2<T>(xv.x * iv * gv.x, xv.y * iv * gv.y);
-          }
-          val = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 xv = tc_unpack2<T>(w[j]), gv = tc_unpack2<T>(gw[j]);
+        w[j] = tc_pack2<T>(xv.x * iv * gv.x, xv.y * iv * gv.y);
       }
-      *reinterpret_cast<uint4*>(xs + static_cast<size_t>(c) * NR * 128 + r * 128 +
-                                ((v ^ (r & 7)) << 4)) = val;
+      *slot = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  // the x slice (written by cp.async and, with NORM, by these threads) is
+  // read by the tensor cores through the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
 
   constexpr uint32_t kIdesc = mma_idesc<T>(NR);
@@ -442,12 +461,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float v[kTiles];
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) {
-      float s = 0.0f;
-      for (int p = 0; p < splits; ++p) {
-        const float* src = part + (t * NR + j) * kTileM + tid;
-        s += splits > 1 ? ld_cluster_f32(src, static_cast<uint32_t>(p)) : *src;
+      const float* src = part + (t * NR + j) * kTileM + tid;
+      if (splits == 1) {
+        v[t] = *src;
+        continue;
       }
-      v[t] = s;
+      float vals[8];  // all peers' values requested first, then summed in rank order
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        vals[p] = p < splits ? ld_cluster_f32(src, static_cast<uint32_t>(p)) : 0.0f;
+      float sum = 0.0f;
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        if (p < splits) sum += vals[p];
+      v[t] = sum;
     }
     hv_keep[jj] = 0.0f;
     if (j >= a.rows) continue;

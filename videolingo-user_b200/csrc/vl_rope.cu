@@ -390,7 +390,10 @@ __global__ void __launch_bounds__(kTileThreads, 4)
   constexpr int NP = P::N;               // packed pairs per 16-byte vector
   constexpr int kHalf = PH * E;          // rotary_dim / 2
   constexpr int TT = kTileTasks / PH;    // tokens per block
-  constexpr int kTable = TT * kHalf;     // = 64 * E entries
+  // table rows padded by 2 floats: the 8-byte reads of the lanes of a warp
+  // (tokens lt, vectors j) then spread over all banks
+  constexpr int kRow = kHalf + 2;
+  constexpr int kTable = TT * kRow;
   __shared__ __align__(16) float cs_c[kTable], cs_s[kTable], cs_n[kTable];
   const int tid = threadIdx.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
@@ -418,21 +421,21 @@ __global__ void __launch_bounds__(kTileThreads, 4)
       x2[g] = ld_vec(p + kHalf + j * E);
     }
   }
-  for (int e = tid; e < kTable; e += kTileThreads) {
+  for (int e = tid; e < TT * kHalf; e += kTileThreads) {
     const int t = e / kHalf, d = e % kHalf;
     const int64_t rr = t0 + t;
     if (rr < a.tokens) {
       const float2 v = rope_cos_sin(static_cast<double>(token_position(a, rr)) * freq.v[d]);
-      cs_c[e] = v.x;
-      cs_s[e] = v.y;
-      cs_n[e] = -v.y;
+      cs_c[t * kRow + d] = v.x;
+      cs_s[t * kRow + d] = v.y;
+      cs_n[t * kRow + d] = -v.y;
     }
   }
   __syncthreads();
   if (!live) return;
-  const f2* tc = reinterpret_cast<const f2*>(cs_c + lt * kHalf + j * E);
-  const f2* ts = reinterpret_cast<const f2*>(cs_s + lt * kHalf + j * E);
-  const f2* tn = reinterpret_cast<const f2*>(cs_n + lt * kHalf + j * E);
+  const f2* tc = reinterpret_cast<const f2*>(cs_c + lt * kRow + j * E);
+  const f2* ts = reinterpret_cast<const f2*>(cs_s + lt * kRow + j * E);
+  const f2* tn = reinterpret_cast<const f2*>(cs_n + lt * kRow + j * E);
   for (int hb = 0; hb < heads; hb += 4 * kTileG) {
     if (hb > 0) {
 #pragma unroll
