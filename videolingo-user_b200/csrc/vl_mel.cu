@@ -17,8 +17,9 @@
 //   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense),
 //     one task per (frame, run of mel bins) with runs of equal cost
 //   log10(max(., 1e-10)) -> out, tile max -> workspace
-// The three stage buffers (samples, stage-1 transpose, packed spectrum)
-// share one 40 KB region, so three tiles fit on an SM.  A second, light
+// The stage-1 transpose and the packed spectrum share one 53 KB region; with
+// the samples (prefetched for the next tile), power spectra and tables a tile
+// takes ~106 KB, two tiles per SM.  A second, light
 // kernel folds the tile maxima of each chunk and applies max(x, max-8) then
 // (x+4)/4 in place.  Chunks are processed in batches whose log-mel (1.5 MB
 // per chunk) stays resident in the 126 MB L2 between the two kernels, so
@@ -52,6 +53,11 @@ constexpr int kTileFrames = 32;            // frames per tile: one per lane in t
 constexpr int kPairs = kTileFrames / 2;    // complex FFTs per tile
 constexpr int kTilesPerChunk = (kFrames + kTileFrames - 1) / kTileFrames;  // 94 (last: 24 frames)
 constexpr int kTileSamples = kHop * (kTileFrames - 1) + 400;  // 5360
+constexpr int kPairSamples = kHop + 400;   // 560: the samples of one frame pair
+// Each pair's samples are kept as their own copy, 564 floats apart: 564 = 20
+// (mod 32), so in stage 1 lane t of a warp reads bank t mod 32 whichever
+// pairs the warp spans (pair offsets 320 p would all start at one bank).
+constexpr int kPairStride = 564;
 constexpr int kBins = 201;
 constexpr int kMel = 128;
 constexpr int kThreads = kPairs * 20;      // 320: one FFT task per thread, 10 warps
@@ -63,16 +69,17 @@ static_assert(kTilesPerChunk <= kMaxTilesPerChunk, "no-alloc scratch too small")
 static_assert(VL_MEL_GROUPS == kThreads / 32, "one mel-bin run per warp");
 
 struct MelSmem {
-  float samples[kTileSamples];             // next tile's samples, filled by cp.async
-  // stage-1 output t[p][k1][n2] -> packed spectra z[p][k]; stage 2 reads t
-  // into registers and passes a barrier before writing z.
+  float samples[kPairs * kPairStride];     // next tile's samples per pair, filled by cp.async
+  // stage-1 output t[p][k1][n2] -> packed spectra z[p][k] -> power spectra
+  // p[frame][bin]; each stage reads the previous one into registers and
+  // passes a barrier before writing the next.
   union {
     float2 t[kPairs][20][kTRow];
     float2 z[kPairs][400];
+    float p[kTileFrames][kBins];
   } u;
-  float p[kTileFrames][kBins];             // power spectra
   float window[400];
-  float2 tw[362];                          // W400^m, m <= 19 * 19
+  float2 tw[20][20];                       // W400^(k1 n2) at [k1][n2]: lanes n2 read consecutive entries
   float red[kThreads / 32];
 };
 
@@ -187,9 +194,16 @@ __device__ __forceinline__ void prefetch_samples(float* dst, const float* __rest
   const float* src = pcm + chunk * kChunkSamples;
   const int j0 = tile * kTileFrames * kHop - kPad;
   if (j0 >= 0 && j0 + kTileSamples <= kChunkSamples) {
-    for (int i = tid; i < kTileSamples / 4; i += kThreads) cp_async16(dst + 4 * i, src + j0 + 4 * i);
+    // pair q: samples j0 + 320 q .. + 560, as 140 16-byte pieces
+    for (int i = tid; i < kPairs * (kPairSamples / 4); i += kThreads) {
+      const int q = i / (kPairSamples / 4), c = i - q * (kPairSamples / 4);
+      cp_async16(dst + q * kPairStride + 4 * c, src + j0 + 2 * kHop * q + 4 * c);
+    }
   } else {
-    for (int i = tid; i < kTileSamples; i += kThreads) cp_async4(dst + i, src + reflect(j0 + i));
+    for (int i = tid; i < kPairs * kPairSamples; i += kThreads) {
+      const int q = i / kPairSamples, c = i - q * kPairSamples;
+      cp_async4(dst + q * kPairStride + c, src + reflect(j0 + 2 * kHop * q + c));
+    }
   }
   cp_async_commit();
 }
@@ -206,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   int w = blockIdx.x;
   if (w < total) prefetch_samples(sm.samples, pcm, chunk0 + w / kTilesPerChunk, w % kTilesPerChunk, tid);
   for (int i = tid; i < 400; i += kThreads) sm.window[i] = mel::kWindow[i];
-  for (int i = tid; i < 362; i += kThreads) sm.tw[i] = mel::kTwiddle400[i];
+  for (int i = tid; i < 400; i += kThreads) sm.tw[i / 20][i % 20] = mel::kTwiddle400[(i / 20) * (i % 20)];
   const int p = tid / 20, lane20 = tid - 20 * (tid / 20);
   const int warp = tid >> 5, lane = tid & 31;
 
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- stage 1: per (pair, n2) DFT-20 over n1 of z[20 n1 + n2], twiddle W400^(k1 n2)
     c2 x[20];
     {
-      const float* sa = sm.samples + 2 * p * kHop;
+      const float* sa = sm.samples + p * kPairStride;
       const float* sb = sa + kHop;
 #pragma unroll
       for (int n1 = 0; n1 < 20; ++n1) {
@@ -237,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     dft20(x);
 #pragma unroll
     for (int k1 = 0; k1 < 20; ++k1) {
-      const float2 tw = sm.tw[k1 * lane20];
+      const float2 tw = sm.tw[k1][lane20];
       *reinterpret_cast<unsigned long long*>(&sm.u.t[p][k1][lane20]) =
           cmul_conj(x[k1], tw.x, tw.y).v;
     }
@@ -254,21 +268,38 @@ __global__ void __launch_bounds__(kThreads, 2)
       *reinterpret_cast<unsigned long long*>(&sm.u.z[p][lane20 + 20 * k2]) = x[k2].v;
     __syncthreads();
 
-    // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i
-    for (int k = lane20; k < kBins; k += 20) {
-      const float2 a = sm.u.z[p][k];
-      const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
-      const float ar = a.x + b.x, ai = a.y - b.y;
-      const float br = a.x - b.x, bi = a.y + b.y;
-      sm.p[2 * p][k] = (ar * ar + ai * ai) * 0.25f;
-      sm.p[2 * p + 1][k] = (br * br + bi * bi) * 0.25f;
+    // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i,
+    // all of this thread's bins into registers, then (the power spectra
+    // overwrite the spectrum) a barrier before they are stored
+    constexpr int kBinSteps = (kBins + 19) / 20;  // 11
+    float pa[kBinSteps], pb[kBinSteps];
+#pragma unroll
+    for (int i = 0; i < kBinSteps; ++i) {
+      const int k = lane20 + 20 * i;
+      if (k < kBins) {
+        const float2 a = sm.u.z[p][k];
+        const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
+        const float ar = a.x + b.x, ai = a.y - b.y;
+        const float br = a.x - b.x, bi = a.y + b.y;
+        pa[i] = (ar * ar + ai * ai) * 0.25f;
+        pb[i] = (br * br + bi * bi) * 0.25f;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kBinSteps; ++i) {
+      const int k = lane20 + 20 * i;
+      if (k < kBins) {
+        sm.u.p[2 * p][k] = pa[i];
+        sm.u.p[2 * p + 1][k] = pb[i];
+      }
     }
     __syncthreads();
 
     // ---- mel projection + log10: warp w = run of bins w, lane = frame
     float local_max = -INFINITY;
     if (f0 + lane < kFrames) {
-      const float* pw = sm.p[lane];
+      const float* pw = sm.u.p[lane];
       float* dst = out + chunk * (static_cast<int64_t>(kMel) * kFrames) + f0 + lane;
       switch (warp) {
         case 0: local_max = mel::mel_run<0>(pw, dst); break;
