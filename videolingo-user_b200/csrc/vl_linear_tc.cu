@@ -41,7 +41,9 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "vl_common.cuh"
 #include "vl_kernels.h"
@@ -173,15 +175,12 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// A float of CTA `rank`'s shared memory at the address of `local` in this
-// CTA.  Only called between cluster barriers (which order it); no memory
-// clobber, so a run of these loads issues back to back.
-__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+// Store a float to CTA `rank`'s shared memory at the address of `local` in
+// this CTA (visible to it after the next cluster barrier).
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(su32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
@@ -426,10 +425,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   tmem_ld_wait();
   if (!finished) atomicExch(bad, 1);
+  // Split-K reduction, push form: token row j belongs to cluster rank
+  // j / rp, which receives every rank's partial of it at
+  // part[((t * rp + j % rp) * splits + rank) * 128 + column]; after one
+  // cluster barrier each CTA sums what it received in rank order, so no CTA
+  // reads another's shared memory and none has to wait for the others to
+  // finish.
+  const int rp = NR / splits;
+  const int lrp = __ffs(rp) - 1;
 #pragma unroll
   for (int t = 0; t < kTiles; ++t)
 #pragma unroll
-    for (int j = 0; j < NR; ++j) part[(t * NR + j) * kTileM + tid] = acc[t][j];
+    for (int j = 0; j < NR; ++j) {
+      const int owner = j >> lrp, jj = j & (rp - 1);
+      float* dst = part + ((t * rp + jj) * splits + static_cast<int>(rank)) * kTileM + tid;
+      if (splits == 1)
+        *dst = acc[t][j];
+      else
+        st_cluster_f32(dst, static_cast<uint32_t>(owner), acc[t][j]);
+    }
   tc_fence_before();
   __syncthreads();
   if (warp == 0)
@@ -446,10 +460,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     atomicAdd(&g_linear_wait_timeouts, 1u);
   }
 
-  // Sum the cluster's partials for this CTA's NR / splits token rows, in
-  // rank order, and finish them.
+  // Sum the partials of this CTA's NR / splits token rows in rank order and
+  // finish them.
   if (splits > 1) cluster_sync();
-  const int rp = NR / splits;
   const int r_begin = static_cast<int>(rank) * rp;
   T* y = static_cast<T*>(a.y);
   float* hbuf = part;  // RESIDUAL: this CTA's new h values, [rp][128], after a barrier
@@ -461,19 +474,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float v[kTiles];
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) {
-      const float* src = part + (t * NR + j) * kTileM + tid;
-      if (splits == 1) {
-        v[t] = *src;
-        continue;
-      }
-      float vals[8];  // all peers' values requested first, then summed in rank order
-#pragma unroll
-      for (int p = 0; p < 8; ++p)
-        vals[p] = p < splits ? ld_cluster_f32(src, static_cast<uint32_t>(p)) : 0.0f;
+      const float* src = part + (t * rp + jj) * splits * kTileM + tid;
       float sum = 0.0f;
-#pragma unroll
-      for (int p = 0; p < 8; ++p)
-        if (p < splits) sum += vals[p];
+      for (int q = 0; q < splits; ++q) sum += src[q * kTileM];
       v[t] = sum;
     }
     hv_keep[jj] = 0.0f;
@@ -492,7 +495,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       hv_keep[jj] = hv;
     }
   }
-  if (splits > 1) cluster_sync();  // every CTA is done reading the others' partials
   if (EPI == VL_LINEAR_RESIDUAL && a.ssq_out != nullptr) {
     __syncthreads();
 #pragma unroll
@@ -544,12 +546,46 @@ int tc_splits(int64_t tiles, int64_t ktiles, int nr) {
   return s;
 }
 
-// Shared memory per CTA such that every CTA of the grid is resident at once
-// (228 KB per SM shared by ceil(ctas / SMs) CTAs), at most kSmemBudget.
-size_t tc_budget(int64_t ctas) {
-  const int64_t per_sm = (ctas + sm_count() - 1) / sm_count();
-  const size_t fit = per_sm > 1 ? static_cast<size_t>(227 * 1024 / per_sm) - 1024 - 2048 : kSmemBudget;
-  return fit < kSmemBudget ? fit : kSmemBudget;
+// Ring depth of a launch: the deepest ring with which every cluster of the
+// grid is resident at once (cudaOccupancyMaxActiveClusters), so no cluster
+// waits for a second wave; cached per (device, kernel, shape).
+int tc_stages(const void* kernel, int nr, int epi, int64_t k, int splits, int64_t clusters) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int64_t, int, int64_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+  const auto key = std::make_tuple(dev, kernel, k, splits, clusters);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int chosen = 1;
+  for (int st = kMaxStages; st >= 1; --st) {
+    const TcLayout L = tc_layout(nr, epi, k, splits, st, kSmemBudget);
+    if (L.stages < st && st > 1) continue;  // this depth does not fit (or exceeds the k tiles)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters), static_cast<unsigned>(splits), 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      break;
+    }
+    chosen = L.stages;
+    if (n >= clusters) break;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = chosen;
+  return chosen;
 }
 
 template <typename T, int NR, int EPI, bool NORM>
@@ -557,19 +593,19 @@ cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cud
   const int64_t cols = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
   const int64_t tiles = cols / kTileM;
   const int splits = tc_splits(tiles, a.k / kTileK, NR);
-  const size_t budget = tc_budget(tiles * splits);
-  const TcLayout L = tc_layout(NR, EPI, a.k, splits, kMaxStages, budget);
   auto kernel = decode_linear_tc_kernel<T, NR, EPI, NORM>;
-  static std::atomic<size_t> configured[64];
+  static std::atomic<bool> configured[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || configured[dev].load(std::memory_order_acquire) < L.total) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBudget + 2048));
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev].store(kSmemBudget + 2048, std::memory_order_release);
+    if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
+  const int stages = tc_stages(reinterpret_cast<const void*>(kernel), NR, EPI, a.k, splits, tiles);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, stages, kSmemBudget);
   cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeClusterDimension;
@@ -589,8 +625,8 @@ cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cud
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kernel, a, map, splits, static_cast<int>(kMaxStages),
-                            static_cast<unsigned int>(budget));
+  return cudaLaunchKernelEx(&cfg, kernel, a, map, splits, stages,
+                            static_cast<unsigned int>(kSmemBudget));
 }
 
 template <typename T, int NR>
@@ -631,9 +667,8 @@ bool decode_linear_tc_supported(const LinearArgs& a, int dtype) {
   if (a.norm_weight != nullptr && !aligned16(a.norm_weight)) return false;
   const int nr = a.rows <= 16 ? 16 : (a.rows <= 32 ? 32 : 64);
   const int splits = tc_splits(cols / kTileM, a.k / kTileK, nr);
-  const size_t budget = tc_budget(cols / kTileM * splits);
-  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, kMaxStages, budget);
-  if (L.stages < 1 || L.total > kSmemBudget + 2048) return false;
+  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, 1, kSmemBudget);
+  if (L.total > kSmemBudget + 2048) return false;
   return encode_fn() != nullptr;
 }
 
