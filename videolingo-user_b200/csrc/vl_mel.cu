@@ -7,19 +7,20 @@
 // max, per-chunk max and the normalise pass (:108-153), with the power and
 // mel spectra making full HBM round trips in between.
 //
-// Here the whole per-frame pipeline is one kernel over tiles of 24 frames:
-//   samples (reflect-padded) -> shared memory
+// Here the whole per-frame pipeline is one kernel over tiles of 32 frames:
+//   samples (reflect-padded) -> shared memory, one copy per frame pair
 //   two real frames packed as one complex 400-point FFT (x_a + i*x_b),
 //     400 = 20 x 20: stage 1 = 20 DFT-20s over stride-20 samples + W400
-//     twiddles, stage 2 = 20 DFT-20s (each DFT-20 = 4 x 5 in registers, in
-//     packed fp32x2 arithmetic: one instruction per complex add/fma)
+//     twiddles, stage 2 = 20 DFT-20s (each DFT-20 a prime-factor 4 x 5 in
+//     registers, in packed fp32x2 arithmetic: one instruction per complex
+//     add/fma)
 //   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry
 //   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense),
 //     one task per (frame, run of mel bins) with runs of equal cost
 //   log10(max(., 1e-10)) -> out, tile max -> workspace
-// The stage-1 transpose and the packed spectrum share one 53 KB region; with
-// the samples (prefetched for the next tile), power spectra and tables a tile
-// takes ~106 KB, two tiles per SM.  A second, light
+// The stage-1 transpose, the packed spectrum and the power spectra share one
+// 53 KB region; with the per-pair samples (prefetched for the next tile) and
+// the tables a tile takes ~93 KB, two tiles per SM.  A second, light
 // kernel folds the tile maxima of each chunk and applies max(x, max-8) then
 // (x+4)/4 in place.  Chunks are processed in batches whose log-mel (1.5 MB
 // per chunk) stays resident in the 126 MB L2 between the two kernels, so
@@ -62,6 +63,9 @@ constexpr int kBins = 201;
 constexpr int kMel = 128;
 constexpr int kThreads = kPairs * 20;      // 320: one FFT task per thread, 10 warps
 constexpr int kTRow = 21;                  // padded row (complex) of the stage-1 transpose
+// padded row (complex) of the packed spectrum: two pairs sharing a warp then
+// start 8 banks apart, the fewest wavefronts for their 8-byte accesses
+constexpr int kZRow = 404;
 constexpr int kNormSlices = 16;            // normalise blocks per chunk
 constexpr int kBatchChunks = 32;           // chunks per L2-resident batch
 constexpr int kMaxTilesPerChunk = 125;     // capacity per chunk of the no-alloc scratch
@@ -75,7 +79,7 @@ struct MelSmem {
   // passes a barrier before writing the next.
   union {
     float2 t[kPairs][20][kTRow];
-    float2 z[kPairs][400];
+    float2 z[kPairs][kZRow];
     float p[kTileFrames][kBins];
   } u;
   float window[400];
