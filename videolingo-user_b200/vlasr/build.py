@@ -66,15 +66,33 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     # Regenerate the mel constant tables (idempotent; rewrites only on change).
     subprocess.run([sys.executable, str(CSRC / "gen_mel_tables.py")], check=True)
     BUILD_DIR.mkdir(exist_ok=True)
-    objs = []
-    for src in sources():
+    # Shared inputs of every object: the headers, generated tables and flags.
+    shared = hashlib.sha256()
+    for q in sorted([*CSRC.glob("*.cuh"), *CSRC.glob("*.h"), *CSRC.glob("*.inc"),
+                     *INCLUDE.glob("*.h")]):
+        shared.update(q.name.encode())
+        shared.update(q.read_bytes())
+    shared.update(" ".join(ARCH_FLAGS + NVCC_FLAGS).encode())
+
+    def compile_one(src: Path) -> str:
+        """Compile one source unless its object is up to date (same source,
+        headers and flags as when it was built)."""
         obj = BUILD_DIR / (src.stem + ".o")
+        key = hashlib.sha256(shared.digest() + src.read_bytes()).hexdigest()
+        sig = obj.with_suffix(".o.sha")
+        if not force and obj.exists() and sig.exists() and sig.read_text() == key:
+            return str(obj)
         cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC),
                "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-        objs.append(str(obj))
+        sig.write_text(key)
+        return str(obj)
+
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as pool:
+        objs = list(pool.map(compile_one, sources()))
     tmp = LIB_PATH.with_suffix(".so.tmp")
     link = [nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs]
     if verbose:
