@@ -546,53 +546,71 @@ int tc_splits(int64_t tiles, int64_t ktiles, int nr) {
   return s;
 }
 
-// Ring depth of a launch: the deepest ring with which every cluster of the
-// grid is resident at once (cudaOccupancyMaxActiveClusters), so no cluster
-// waits for a second wave; cached per (device, kernel, shape).
-int tc_stages(const void* kernel, int nr, int epi, int64_t k, int splits, int64_t clusters) {
+// Split count and ring depth of a launch, chosen together: clusters of 8
+// CTAs are scarce on this part (cudaOccupancyMaxActiveClusters reports 15 on
+// a B200 whatever a CTA's shared memory), so a grid of more clusters than
+// can be resident runs in two waves.  Search the split counts from the one
+// that gives every SM a CTA (tc_splits) down to 1 and take the first whose
+// clusters are all resident, with the deepest ring that keeps them so; if
+// none is, the largest split with its deepest ring.  Cached per (device,
+// kernel, shape).
+struct TcPlan {
+  int splits;
+  int stages;
+};
+
+TcPlan tc_plan(const void* kernel, int nr, int epi, int64_t k, int64_t tiles) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int64_t, int, int64_t>, int> cache;
+  static std::map<std::tuple<int, const void*, int64_t, int64_t>, TcPlan> cache;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
-  const auto key = std::make_tuple(dev, kernel, k, splits, clusters);
+  if (cudaGetDevice(&dev) != cudaSuccess) return TcPlan{1, 1};
+  const auto key = std::make_tuple(dev, kernel, k, tiles);
   {
     std::lock_guard<std::mutex> lock(mu);
     const auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  int chosen = 1;
-  for (int st = kMaxStages; st >= 1; --st) {
-    const TcLayout L = tc_layout(nr, epi, k, splits, st, kSmemBudget);
-    if (L.stages < st && st > 1) continue;  // this depth does not fit (or exceeds the k tiles)
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = static_cast<unsigned>(splits);
-    attr[0].val.clusterDim.z = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(clusters), static_cast<unsigned>(splits), 1);
-    cfg.blockDim = dim3(kTcThreads, 1, 1);
-    cfg.dynamicSmemBytes = L.total;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
-      (void)cudaGetLastError();
-      break;
+  const int64_t ktiles = k / kTileK;
+  TcPlan best{0, 0}, fallback{0, 0};
+  for (int sp = tc_splits(tiles, ktiles, nr); sp >= 1 && best.splits == 0; sp /= 2) {
+    if (ktiles % sp != 0 || nr / sp < 1) continue;
+    for (int st = kMaxStages; st >= 1; --st) {
+      const TcLayout L = tc_layout(nr, epi, k, sp, st, kSmemBudget);
+      if (L.total > kSmemBudget + 2048) continue;       // does not fit at all
+      if (L.stages < st && st > 1) continue;            // this depth does not fit
+      if (fallback.splits == 0) fallback = TcPlan{sp, L.stages};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = static_cast<unsigned>(sp);
+      attr[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(sp), 1);
+      cfg.blockDim = dim3(kTcThreads, 1, 1);
+      cfg.dynamicSmemBytes = L.total;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        continue;
+      }
+      if (n >= tiles) {
+        best = TcPlan{sp, L.stages};
+        break;
+      }
     }
-    chosen = L.stages;
-    if (n >= clusters) break;
   }
+  if (best.splits == 0) best = fallback.splits != 0 ? fallback : TcPlan{1, 1};
   std::lock_guard<std::mutex> lock(mu);
-  cache[key] = chosen;
-  return chosen;
+  cache[key] = best;
+  return best;
 }
 
 template <typename T, int NR, int EPI, bool NORM>
 cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cudaStream_t stream) {
   const int64_t cols = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : a.n;
   const int64_t tiles = cols / kTileM;
-  const int splits = tc_splits(tiles, a.k / kTileK, NR);
   auto kernel = decode_linear_tc_kernel<T, NR, EPI, NORM>;
   static std::atomic<bool> configured[64];
   int dev = 0;
@@ -604,7 +622,8 @@ cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cud
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
-  const int stages = tc_stages(reinterpret_cast<const void*>(kernel), NR, EPI, a.k, splits, tiles);
+  const TcPlan plan = tc_plan(reinterpret_cast<const void*>(kernel), NR, EPI, a.k, tiles);
+  const int splits = plan.splits, stages = plan.stages;
   const TcLayout L = tc_layout(NR, EPI, a.k, splits, stages, kSmemBudget);
   cudaLaunchAttribute attr[2];
   int na = 0;
@@ -666,9 +685,12 @@ bool decode_linear_tc_supported(const LinearArgs& a, int dtype) {
   if (!aligned16(a.w) || !aligned16(a.x) || a.x_row_stride % 8 != 0) return false;
   if (a.norm_weight != nullptr && !aligned16(a.norm_weight)) return false;
   const int nr = a.rows <= 16 ? 16 : (a.rows <= 32 ? 32 : 64);
-  const int splits = tc_splits(cols / kTileM, a.k / kTileK, nr);
-  const TcLayout L = tc_layout(nr, a.epilogue, a.k, splits, 1, kSmemBudget);
-  if (L.total > kSmemBudget + 2048) return false;
+  // some split count must fit one k tile per stage
+  bool fits = false;
+  for (int sp = tc_splits(cols / kTileM, a.k / kTileK, nr); sp >= 1 && !fits; sp /= 2)
+    fits = (a.k / kTileK) % sp == 0 &&
+           tc_layout(nr, a.epilogue, a.k, sp, 1, kSmemBudget).total <= kSmemBudget + 2048;
+  if (!fits) return false;
   return encode_fn() != nullptr;
 }
 

@@ -289,193 +289,6 @@ __global__ void __launch_bounds__(kWarpRopeWarps * 32)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Tile kernel for many tokens (prefill, encoder): 256 threads own 64 / PH
-// tokens, so task i = ((h * T) + t) * PH + j decomposes with shifts, and the
-// GMAX tasks of one thread (heads h, h + 4, h + 8, ...) share its token t and
-// vector j - hence its 8 cos/sin pairs, read once from the block's table.
-// All of a thread's vectors are requested before the table is built; the
-// rotation runs in packed fp32x2 instructions with the oracle's rounding:
-// y1 = fma(x1, c, x2 * -s), y2 = fma(x2, c, x1 * s).
-// ---------------------------------------------------------------------------
-constexpr int kTileThreads = 256;
-constexpr int kTileTasks = 64;   // tokens per block x rotated vectors per head
-constexpr int kTileG = 5;        // heads per thread per round (20 heads per round)
-
-struct f2 {
-  unsigned long long v;
-};
-__device__ __forceinline__ f2 f2_make(float lo, float hi) {
-  f2 r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ float2 f2_split(f2 a) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a.v));
-  return r;
-}
-__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
-  f2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
-  f2 r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
-  return r;
-}
-
-// 16-byte vector <-> E/2 packed pairs of floats, per storage type.
-template <typename T>
-struct Pairs;
-template <>
-struct Pairs<__nv_bfloat16> {
-  static constexpr int N = 4;
-  static __device__ __forceinline__ void unpack(const uint4& v, f2 (&p)[4]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) p[i] = f2_make(bf16_lo(w[i]), bf16_hi(w[i]));
-  }
-  static __device__ __forceinline__ uint4 pack(const f2 (&p)[4]) {
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = f2_split(p[i]);
-      w[i] = pack_bf16x2(f.x, f.y);
-    }
-    return make_uint4(w[0], w[1], w[2], w[3]);
-  }
-};
-template <>
-struct Pairs<__half> {
-  static constexpr int N = 4;
-  static __device__ __forceinline__ void unpack(const uint4& v, f2 (&p)[4]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-      p[i] = f2_make(f.x, f.y);
-    }
-  }
-  static __device__ __forceinline__ uint4 pack(const f2 (&p)[4]) {
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = f2_split(p[i]);
-      w[i] = pack_f16x2(f.x, f.y);
-    }
-    return make_uint4(w[0], w[1], w[2], w[3]);
-  }
-};
-template <>
-struct Pairs<float> {
-  static constexpr int N = 2;
-  static __device__ __forceinline__ void unpack(const uint4& v, f2 (&p)[2]) {
-    p[0] = f2_make(__uint_as_float(v.x), __uint_as_float(v.y));
-    p[1] = f2_make(__uint_as_float(v.z), __uint_as_float(v.w));
-  }
-  static __device__ __forceinline__ uint4 pack(const f2 (&p)[2]) {
-    const float2 a = f2_split(p[0]), b = f2_split(p[1]);
-    return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
-                      __float_as_uint(b.y));
-  }
-};
-
-template <typename T, int PH>
-__global__ void __launch_bounds__(kTileThreads, 4)
-    rope_tile_kernel(const __grid_constant__ RopeArgs a, const __grid_constant__ InvFreq freq) {
-  using P = Pairs<T>;
-  constexpr int E = Storage<T>::kVec;
-  constexpr int NP = P::N;               // packed pairs per 16-byte vector
-  constexpr int kHalf = PH * E;          // rotary_dim / 2
-  constexpr int TT = kTileTasks / PH;    // tokens per block
-  // table rows padded by 2 floats: the 8-byte reads of the lanes of a warp
-  // (tokens lt, vectors j) then spread over all banks
-  constexpr int kRow = kHalf + 2;
-  constexpr int kTable = TT * kRow;
-  __shared__ __align__(16) float cs_c[kTable], cs_s[kTable], cs_n[kTable];
-  const int tid = threadIdx.x;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
-  const int lt = (tid & (kTileTasks - 1)) / PH;   // this thread's token in the tile
-  const int j = tid & (PH - 1);                   // and rotated vector
-  const int h0 = tid / kTileTasks;                // first head (then + 4 per task)
-  const int64_t r = t0 + lt;
-  const bool live = r < a.tokens;
-  const int heads = a.n_q_heads + a.n_k_heads;
-  T* qrow = static_cast<T*>(a.q) + r * a.q_row_stride;
-  T* krow = static_cast<T*>(a.k) + r * a.k_row_stride;
-  auto head = [&](int h) {
-    return h < a.n_q_heads ? qrow + static_cast<int64_t>(h) * a.head_dim
-                           : krow + static_cast<int64_t>(h - a.n_q_heads) * a.head_dim;
-  };
-
-  uint4 x1[kTileG], x2[kTileG];
-  // first round of vectors, before the table
-#pragma unroll
-  for (int g = 0; g < kTileG; ++g) {
-    const int h = h0 + 4 * g;
-    if (live && h < heads) {
-      T* p = head(h);
-      x1[g] = ld_vec(p + j * E);
-      x2[g] = ld_vec(p + kHalf + j * E);
-    }
-  }
-  for (int e = tid; e < TT * kHalf; e += kTileThreads) {
-    const int t = e / kHalf, d = e % kHalf;
-    const int64_t rr = t0 + t;
-    if (rr < a.tokens) {
-      const float2 v = rope_cos_sin(static_cast<double>(token_position(a, rr)) * freq.v[d]);
-      cs_c[t * kRow + d] = v.x;
-      cs_s[t * kRow + d] = v.y;
-      cs_n[t * kRow + d] = -v.y;
-    }
-  }
-  __syncthreads();
-  if (!live) return;
-  const f2* tc = reinterpret_cast<const f2*>(cs_c + lt * kRow + j * E);
-  const f2* ts = reinterpret_cast<const f2*>(cs_s + lt * kRow + j * E);
-  const f2* tn = reinterpret_cast<const f2*>(cs_n + lt * kRow + j * E);
-  for (int hb = 0; hb < heads; hb += 4 * kTileG) {
-    if (hb > 0) {
-#pragma unroll
-      for (int g = 0; g < kTileG; ++g) {
-        const int h = hb + h0 + 4 * g;
-        if (h < heads) {
-          T* p = head(h);
-          x1[g] = ld_vec(p + j * E);
-          x2[g] = ld_vec(p + kHalf + j * E);
-        }
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < kTileG; ++g) {
-      const int h = hb + h0 + 4 * g;
-      if (h < heads) {
-        f2 a1[NP], a2[NP], y1[NP], y2[NP];
-        P::unpack(x1[g], a1);
-        P::unpack(x2[g], a2);
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
-          const f2 c = tc[i];
-          y1[i] = f2_fma(a1[i], c, f2_mul(a2[i], tn[i]));
-          y2[i] = f2_fma(a2[i], c, f2_mul(a1[i], ts[i]));
-        }
-        T* p = head(h);
-        st_vec(p + j * E, P::pack(y1));
-        st_vec(p + kHalf + j * E, P::pack(y2));
-      }
-    }
-  }
-}
-
-template <typename T, int PH>
-void launch_tile_rope(const RopeArgs& a, const InvFreq& freq, cudaStream_t stream) {
-  constexpr int TT = kTileTasks / PH;
-  const int64_t blocks = (a.tokens + TT - 1) / TT;
-  rope_tile_kernel<T, PH><<<static_cast<unsigned>(blocks), kTileThreads, 0, stream>>>(a, freq);
-}
-
 template <typename T, int PH>
 void launch_warp_rope(const RopeArgs& a, const InvFreq& freq, cudaStream_t stream) {
   const int64_t need = (a.tokens + kWarpRopeWarps - 1) / kWarpRopeWarps;
@@ -505,19 +318,7 @@ cudaError_t rope_typed(const RopeArgs& a, cudaStream_t stream) {
   const int64_t blocks = (a.tokens + tpb - 1) / tpb;
   const size_t smem = static_cast<size_t>(tpb) * half_rot * sizeof(float2);
   const int per_head = half_rot / E;
-  // Many tokens without the fused append: the tile kernel (one wave of
-  // blocks of 64 / PH tokens); few tokens or the decode-step fusion: the
-  // persistent warp kernel.
-  if (vec && a.v == nullptr && per_head <= 16 && (per_head & (per_head - 1)) == 0 &&
-      a.tokens >= 8 * static_cast<int64_t>(sm_count())) {
-    switch (per_head) {
-      case 1: launch_tile_rope<T, 1>(a, freq, stream); break;
-      case 2: launch_tile_rope<T, 2>(a, freq, stream); break;
-      case 4: launch_tile_rope<T, 4>(a, freq, stream); break;
-      case 8: launch_tile_rope<T, 8>(a, freq, stream); break;
-      default: launch_tile_rope<T, 16>(a, freq, stream); break;
-    }
-  } else if (vec && per_head <= 32 && (per_head & (per_head - 1)) == 0) {
+  if (vec && per_head <= 32 && (per_head & (per_head - 1)) == 0) {
     switch (per_head) {
       case 1: launch_warp_rope<T, 1>(a, freq, stream); break;
       case 2: launch_warp_rope<T, 2>(a, freq, stream); break;
