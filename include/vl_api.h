@@ -485,13 +485,14 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
  * norm_weight 16-byte aligned with row strides that are multiples of 8 elements, x not
  * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
  * flags: 0 or VL_LAUNCH_PDL.
- * Kernels: when the output columns (n, or n/2 for SWIGLU) are a multiple of
- * 128, the 5th-generation tensor cores compute it (tcgen05.mma with the
- * accumulator in tensor memory, weights streamed by TMA, K split over a
- * thread-block cluster whose partial sums meet in distributed shared
- * memory); other shapes use a tensor-core kernel of the previous generation
- * (mma.sync).  Both keep the rounding points above; their fp32 summation
- * orders differ, each is deterministic.
+ * Kernels: from 17 rows, when the output columns (n, or n/2 for SWIGLU)
+ * are a multiple of 128, the 5th-generation tensor cores compute it
+ * (tcgen05.mma with the accumulator in tensor memory, weights streamed by
+ * TMA, K split over a thread-block cluster whose partial sums meet in
+ * distributed shared memory); up to 16 rows and for other shapes a
+ * tensor-core kernel of the previous generation (mma.sync), which spreads a
+ * few-row weight stream over more SMs.  Both keep the rounding points
+ * above; their fp32 summation orders differ, each is deterministic.
  */
 #define VL_LINEAR_STORE 0
 #define VL_LINEAR_SWIGLU 1

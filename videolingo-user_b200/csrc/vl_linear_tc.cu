@@ -59,7 +59,7 @@ constexpr int kTcThreads = 128;
 constexpr int kTileM = 128;                 // output columns per CTA (MMA M)
 constexpr int kTileK = 64;                  // k per stage: 64 x 2 B = one 128-byte swizzle row
 constexpr int kTileBytes = kTileM * kTileK * 2;  // 16 KB per weight tile
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 8;
 constexpr size_t kSmemBudget = 220 * 1024;
 constexpr uint32_t kWaitLimit = 1u << 22;   // try_wait polls before a wait gives up (~seconds)
 
@@ -216,24 +216,26 @@ struct TcLayout {
   size_t ring;       // bytes
   size_t xs;         // bytes of the x slice
   size_t part;       // bytes of the partial accumulators
+  size_t norm;       // RMSNorm prologue: the partial sums [k/16][rows] and this CTA's norm weights
   size_t total;      // dynamic shared memory (incl. 1 KB alignment slack)
 };
 
 // budget: shared memory one CTA may take (so that the grid's CTAs are
 // resident in one wave, see tc_budget).
 __host__ __device__ inline TcLayout tc_layout(int nr, int epi, int64_t k, int splits,
-                                              int max_stages, size_t budget) {
+                                              int max_stages, size_t budget, bool norm) {
   TcLayout L{};
   L.chunks = static_cast<int>(k / kTileK / splits);
   const int tiles = epi == VL_LINEAR_SWIGLU ? 2 : 1;
   L.xs = static_cast<size_t>(nr) * 128 * L.chunks;
   L.part = static_cast<size_t>(tiles) * nr * kTileM * 4;
+  L.norm = norm ? static_cast<size_t>(k / 16) * nr * 4 + static_cast<size_t>(L.chunks) * 128 : 0;
   L.stages = L.chunks < max_stages ? L.chunks : max_stages;
-  while (L.stages > 1 &&
-         static_cast<size_t>(L.stages) * tiles * kTileBytes + L.xs + L.part + 2048 > budget)
+  while (L.stages > 1 && static_cast<size_t>(L.stages) * tiles * kTileBytes + L.xs + L.part +
+                                 L.norm + 2048 > budget)
     --L.stages;
   L.ring = static_cast<size_t>(L.stages) * tiles * kTileBytes;
-  L.total = L.ring + L.xs + L.part + 1024 /*align*/ + 1024 /*barriers, tmem slot, inv*/;
+  L.total = L.ring + L.xs + L.part + L.norm + 1024 /*align*/ + 1024 /*barriers, tmem slot, inv*/;
   return L;
 }
 
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr int kTiles = EPI == VL_LINEAR_SWIGLU ? 2 : 1;
   constexpr int kAccCols = kTiles * NR;
   constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : 128);
-  const TcLayout L = tc_layout(NR, EPI, a.k, splits, max_stages, budget);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, max_stages, budget, NORM);
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -254,7 +256,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   unsigned char* ring = base;
   unsigned char* xs = ring + L.ring;
   float* part = reinterpret_cast<float*>(xs + L.xs);  // [kTiles][NR][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(part) + L.part);
+  // NORM: the producer's partial sums of squares [k/16][rows], then this
+  // CTA's k slice of the norm weight
+  float* ssq_s = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(part) + L.part);
+  T* gam_s = reinterpret_cast<T*>(ssq_s + (NORM ? (a.k / 16) * NR : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(part) + L.part +
+                                               L.norm);
   uint64_t* full = bars;                    // [stages]
   uint64_t* empty = bars + kMaxStages;      // [stages]
   uint64_t* done = bars + 2 * kMaxStages;
@@ -269,6 +276,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t kbase = static_cast<int64_t>(rank) * L.chunks * kTileK;
   const int64_t up_row = EPI == VL_LINEAR_SWIGLU ? a.n / 2 : 0;
 
+  // Weight tile c into ring stage c % stages (thread 0).
+  auto issue = [&](int c) {
+    const int s = c % L.stages;
+    unsigned char* dst = ring + static_cast<size_t>(s) * kTiles * kTileBytes;
+    mbar_expect_tx(&full[s], kTiles * kTileBytes);
+    const int kx = static_cast<int>(kbase + static_cast<int64_t>(c) * kTileK);
+    tma_load_2d(dst, &wmap, kx, static_cast<int>(col0), &full[s]);
+    if (EPI == VL_LINEAR_SWIGLU)
+      tma_load_2d(dst + kTileBytes, &wmap, kx, static_cast<int>(up_row + col0), &full[s]);
+  };
+  int issued = 0;  // producer (thread 0): weight tiles requested so far
   if (tid == 0) {
     for (int s = 0; s < L.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -278,7 +296,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     *bad = 0;
     *issued_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the first stages' weight tiles go out at once, before the tensor
+    // memory allocation and the dependency wait (weights never depend on the
+    // previous kernel)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    for (; issued < L.stages; ++issued) issue(issued);
   }
+  __syncwarp();
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      su32(tmem_slot)),
@@ -291,20 +315,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Weight tiles of the first stages: issued before the dependency wait.
-  auto issue = [&](int c) {
-    const int s = c % L.stages;
-    unsigned char* dst = ring + static_cast<size_t>(s) * kTiles * kTileBytes;
-    mbar_expect_tx(&full[s], kTiles * kTileBytes);
-    const int kx = static_cast<int>(kbase + static_cast<int64_t>(c) * kTileK);
-    tma_load_2d(dst, &wmap, kx, static_cast<int>(col0), &full[s]);
-    if (EPI == VL_LINEAR_SWIGLU)
-      tma_load_2d(dst + kTileBytes, &wmap, kx, static_cast<int>(up_row + col0), &full[s]);
-  };
-  int issued = 0;  // producer (thread 0): weight tiles requested so far
-  if (tid == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
-    for (; issued < L.stages; ++issued) issue(issued);
+  if (NORM) {  // the norm weight is a model input: fetched before the dependency wait
+    const T* gam = static_cast<const T*>(a.norm_weight) + kbase;
+    for (int i = tid; i < L.chunks * 8; i += kTcThreads) cp_async16_zfill(gam_s + 8 * i, gam + 8 * i, true);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   pdl_wait();
   pdl_release();
@@ -323,8 +337,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       cp_async16_zfill(xs + static_cast<size_t>(c) * NR * 128 + r * 128 + ((v ^ (r & 7)) << 4),
                        x + (ok ? r : 0) * a.x_row_stride + kk, ok);
     }
+    if (NORM) {  // the producer's partial sums, [parts][rows] as one contiguous block
+      const int nf = a.ssq_in_parts * static_cast<int>(a.rows);
+      if ((reinterpret_cast<uintptr_t>(a.ssq_in) & 15) == 0 && nf % 4 == 0) {
+        for (int i = tid; i < nf / 4; i += kTcThreads) cp_async16_zfill(ssq_s + 4 * i, a.ssq_in + 4 * i, true);
+      } else {
+        for (int i = tid; i < nf; i += kTcThreads) ssq_s[i] = a.ssq_in[i];
+      }
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
   // RMSNorm prologue: 1 / rms of every row from the producer's partial sums
   // (a warp per row, lane l sums parts l, l+32, ... in order, then a fixed
   // xor tree), the same order as vl_linear.cu; then x = round(x * inv * w)
@@ -332,17 +356,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (NORM) {
     for (int r = warp; r < a.rows; r += kTcThreads / 32) {
       float ssq = 0.0f;
-      for (int p = lane; p < a.ssq_in_parts; p += 32)
-        ssq += a.ssq_in[static_cast<int64_t>(p) * a.rows + r];
+      for (int p = lane; p < a.ssq_in_parts; p += 32) ssq += ssq_s[p * a.rows + r];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
       if (lane == 0) inv_s[r] = rsqrtf(ssq / static_cast<float>(a.k) + a.eps);
     }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   if (NORM) {
-    const T* gam = static_cast<const T*>(a.norm_weight);
     for (int i = tid; i < nvec; i += kTcThreads) {
       const int v = i & 7, r = (i >> 3) % NR, c = (i >> 3) / NR;
       if (r >= a.rows) continue;
@@ -350,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint4* slot = reinterpret_cast<uint4*>(xs + static_cast<size_t>(c) * NR * 128 + r * 128 +
                                              ((v ^ (r & 7)) << 4));
       const uint4 val = *slot;
-      const uint4 g = __ldg(reinterpret_cast<const uint4*>(gam + kk));
+      const uint4 g = *reinterpret_cast<const uint4*>(gam_s + (kk - kbase));
       const float iv = inv_s[r];
       uint32_t w[4] = {val.x, val.y, val.z, val.w};
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
@@ -465,35 +486,58 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (splits > 1) cluster_sync();
   const int r_begin = static_cast<int>(rank) * rp;
   T* y = static_cast<T*>(a.y);
+  const bool ok = !*reinterpret_cast<volatile int*>(bad);  // read once, before any store
   float* hbuf = part;  // RESIDUAL: this CTA's new h values, [rp][128], after a barrier
   float hv_keep[NR];
+  // RESIDUAL: every old h value of this thread is requested before any new
+  // one is stored (a store could alias the next row's load otherwise, which
+  // would serialise the rows)
+  float h_old[EPI == VL_LINEAR_RESIDUAL ? NR : 1];
+  if (EPI == VL_LINEAR_RESIDUAL) {
+#pragma unroll
+    for (int jj = 0; jj < NR; ++jj) {
+      const int j = r_begin + jj;
+      h_old[jj] = (jj < rp && j < a.rows) ? S::to_float(y[j * a.y_row_stride + col0 + tid]) : 0.0f;
+    }
+  }
+  // All of this thread's rows are summed and finished first, then stored:
+  // a partial-sum load issued after a global store waits for it, which cost
+  // about a microsecond per row when the two alternated.
+  float outv[NR];
 #pragma unroll
   for (int jj = 0; jj < NR; ++jj) {
-    if (jj >= rp) break;
-    const int j = r_begin + jj;
+    outv[jj] = 0.0f;
+    hv_keep[jj] = 0.0f;
+    if (jj >= rp) continue;
     float v[kTiles];
 #pragma unroll
     for (int t = 0; t < kTiles; ++t) {
       const float* src = part + (t * rp + jj) * splits * kTileM + tid;
       float sum = 0.0f;
-      for (int q = 0; q < splits; ++q) sum += src[q * kTileM];
+      for (int q = 0; q < splits; ++q) {  // explicit shared-memory loads (measured faster)
+        float pv;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(pv) : "r"(su32(src + q * kTileM)));
+        sum += pv;
+      }
       v[t] = sum;
     }
-    hv_keep[jj] = 0.0f;
-    if (j >= a.rows) continue;
-    T* dst = y + j * a.y_row_stride + col0 + tid;
-    const bool ok = !*reinterpret_cast<volatile int*>(bad);
     if (EPI == VL_LINEAR_STORE) {
-      *dst = S::from_float(ok ? v[0] : __int_as_float(0x7fc00000));
+      outv[jj] = v[0];
     } else if (EPI == VL_LINEAR_SWIGLU) {
       const float g = S::round_trip(v[0]);
       const float u = S::round_trip(v[kTiles - 1]);
-      *dst = S::from_float(ok ? __fdividef(g, 1.0f + __expf(-g)) * u : __int_as_float(0x7fc00000));
+      outv[jj] = __fdividef(g, 1.0f + __expf(-g)) * u;
     } else {
-      const float hv = S::round_trip(S::to_float(*dst) + S::round_trip(v[0]));
-      *dst = S::from_float(ok ? hv : __int_as_float(0x7fc00000));
+      const float hv = S::round_trip(h_old[EPI == VL_LINEAR_RESIDUAL ? jj : 0] + S::round_trip(v[0]));
+      outv[jj] = hv;
       hv_keep[jj] = hv;
     }
+  }
+#pragma unroll
+  for (int jj = 0; jj < NR; ++jj) {
+    const int j = r_begin + jj;
+    if (jj < rp && j < a.rows)
+      y[j * a.y_row_stride + col0 + tid] = S::from_float(ok ? outv[jj] : __int_as_float(0x7fc00000));
   }
   if (EPI == VL_LINEAR_RESIDUAL && a.ssq_out != nullptr) {
     __syncthreads();
@@ -559,7 +603,7 @@ struct TcPlan {
   int stages;
 };
 
-TcPlan tc_plan(const void* kernel, int nr, int epi, int64_t k, int64_t tiles) {
+TcPlan tc_plan(const void* kernel, int nr, int epi, bool norm, int64_t k, int64_t tiles) {
   static std::mutex mu;
   static std::map<std::tuple<int, const void*, int64_t, int64_t>, TcPlan> cache;
   int dev = 0;
@@ -575,7 +619,7 @@ TcPlan tc_plan(const void* kernel, int nr, int epi, int64_t k, int64_t tiles) {
   for (int sp = tc_splits(tiles, ktiles, nr); sp >= 1 && best.splits == 0; sp /= 2) {
     if (ktiles % sp != 0 || nr / sp < 1) continue;
     for (int st = kMaxStages; st >= 1; --st) {
-      const TcLayout L = tc_layout(nr, epi, k, sp, st, kSmemBudget);
+      const TcLayout L = tc_layout(nr, epi, k, sp, st, kSmemBudget, norm);
       if (L.total > kSmemBudget + 2048) continue;       // does not fit at all
       if (L.stages < st && st > 1) continue;            // this depth does not fit
       if (fallback.splits == 0) fallback = TcPlan{sp, L.stages};
@@ -622,9 +666,9 @@ cudaError_t tc_launch(const LinearArgs& a, const CUtensorMap& map, bool pdl, cud
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
-  const TcPlan plan = tc_plan(reinterpret_cast<const void*>(kernel), NR, EPI, a.k, tiles);
+  const TcPlan plan = tc_plan(reinterpret_cast<const void*>(kernel), NR, EPI, NORM, a.k, tiles);
   const int splits = plan.splits, stages = plan.stages;
-  const TcLayout L = tc_layout(NR, EPI, a.k, splits, stages, kSmemBudget);
+  const TcLayout L = tc_layout(NR, EPI, a.k, splits, stages, kSmemBudget, NORM);
   cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeClusterDimension;
@@ -684,12 +728,15 @@ bool decode_linear_tc_supported(const LinearArgs& a, int dtype) {
   if (a.n > (int64_t(1) << 31) - 1 || a.k > (int64_t(1) << 31) - 1) return false;
   if (!aligned16(a.w) || !aligned16(a.x) || a.x_row_stride % 8 != 0) return false;
   if (a.norm_weight != nullptr && !aligned16(a.norm_weight)) return false;
+  // the RMSNorm prologue stages the partial sums in a [k/16][rows] buffer
+  if (a.norm_weight != nullptr && (a.ssq_in_parts < 1 || a.ssq_in_parts > a.k / 16)) return false;
   const int nr = a.rows <= 16 ? 16 : (a.rows <= 32 ? 32 : 64);
   // some split count must fit one k tile per stage
   bool fits = false;
   for (int sp = tc_splits(cols / kTileM, a.k / kTileK, nr); sp >= 1 && !fits; sp /= 2)
     fits = (a.k / kTileK) % sp == 0 &&
-           tc_layout(nr, a.epilogue, a.k, sp, 1, kSmemBudget).total <= kSmemBudget + 2048;
+           tc_layout(nr, a.epilogue, a.k, sp, 1, kSmemBudget, a.norm_weight != nullptr).total <=
+               kSmemBudget + 2048;
   if (!fits) return false;
   return encode_fn() != nullptr;
 }

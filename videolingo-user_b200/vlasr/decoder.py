@@ -47,10 +47,10 @@ from ._lib import VlasrInputError
 EOS_IDS = (59246, 59253, 59255)
 AUDIO_TOKEN_ID = 59260
 AUDIO_TOKENS_PER_CHUNK = 375
-# Decode steps of up to this many chunks run the fused layers (one 16-row
-# tile of vl_decode_linear per weight stream); larger batches run cuBLAS
-# GEMMs, which reuse each weight tile across more rows.
-FUSED_MAX_ROWS = 16
+# Decode steps of up to this many chunks run the fused layers through
+# vl_decode_linear (its mma.sync kernel up to 16 rows, its tcgen05 kernel
+# from 17 to 64); larger batches run cuBLAS GEMMs.
+FUSED_MAX_ROWS = 64
 
 
 @dataclass(frozen=True)

@@ -176,14 +176,17 @@ class PeerPushGather:
         dist.barrier(group=self.group)
 
 
+EDGE_MAX_CHUNKS = 4
+
+
 def host_group_bounds(chunks: int, groups: int) -> list[tuple[int, int]]:
     """Chunk groups of the host-buffer pipeline: `groups` equal middle groups
-    plus a half-size first and last group, so the upload that nothing
-    overlaps (the first) and the download that nothing overlaps (the last)
-    are short."""
+    plus a small first and last group (half a middle group, at most
+    EDGE_MAX_CHUNKS chunks), so the upload that nothing overlaps (the first)
+    and the download that nothing overlaps (the last) are short."""
     if groups <= 1 or chunks < 4:
         return [(0, chunks)]
-    edge = max(1, chunks // (2 * groups))
+    edge = max(1, min(EDGE_MAX_CHUNKS, chunks // (2 * groups)))
     inner = [shard_range(chunks - 2 * edge, g, groups - 1) for g in range(groups - 1)]
     bounds = [(0, edge)] + [(edge + a, edge + b) for a, b in inner if b > a]
     bounds.append((chunks - edge, chunks))
