@@ -48,9 +48,10 @@ EOS_IDS = (59246, 59253, 59255)
 AUDIO_TOKEN_ID = 59260
 AUDIO_TOKENS_PER_CHUNK = 375
 # Decode steps of up to this many chunks run the fused layers through
-# vl_decode_linear (its mma.sync kernel up to 16 rows, its tcgen05 kernel
-# from 17 to 64); larger batches run cuBLAS GEMMs.
-FUSED_MAX_ROWS = 64
+# vl_decode_linear (its mma.sync kernel); larger batches run cuBLAS GEMMs,
+# which measured faster per launch than either kernel of vl_decode_linear
+# from 17 rows up.
+FUSED_MAX_ROWS = 16
 
 
 @dataclass(frozen=True)
