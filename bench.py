@@ -71,11 +71,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--nccl-channels", type=int, default=None,
                    help="cap NCCL's channels (and so the SMs its all-gather occupies "
                         "while it overlaps the next step's kernels)")
-    p.add_argument("--gather", choices=["copy", "nccl", "blocking"], default="copy",
+    p.add_argument("--gather", choices=["copy", "nccl", "blocking"], default="nccl",
                    help="all-gather of each step's outputs: copy-engine pushes into every "
-                        "rank's buffer overlapping the next step (default), an NCCL all-gather "
-                        "on a side stream overlapping the next step, or NCCL at the end of "
-                        "the step")
+                        "rank's buffer overlapping the next step, an NCCL all-gather on a "
+                        "side stream overlapping the next step (default), or NCCL at the end "
+                        "of the step")
     p.add_argument("--encoder", action="store_true",
                    help="encoder mode: the GLM-ASR audio tower + projector (vlasr.encoder) on a "
                         "seeded synthetic checkpoint; with --impl reference, the reference's own "
