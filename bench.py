@@ -71,11 +71,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--nccl-channels", type=int, default=None,
                    help="cap NCCL's channels (and so the SMs its all-gather occupies "
                         "while it overlaps the next step's kernels)")
-    p.add_argument("--gather", choices=["copy", "nccl", "blocking"], default="nccl",
+    p.add_argument("--gather", choices=["copy", "nccl", "blocking"], default="copy",
                    help="all-gather of each step's outputs: copy-engine pushes into every "
-                        "rank's buffer overlapping the next step, an NCCL all-gather on a "
-                        "side stream overlapping the next step (default), or NCCL at the end "
-                        "of the step")
+                        "rank's buffer overlapping the next step (default), an NCCL all-gather "
+                        "on a side stream overlapping the next step, or NCCL at the end of "
+                        "the step")
     p.add_argument("--encoder", action="store_true",
                    help="encoder mode: the GLM-ASR audio tower + projector (vlasr.encoder) on a "
                         "seeded synthetic checkpoint; with --impl reference, the reference's own "
@@ -345,6 +345,15 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         return ("Q [4,2048,16,128] K [4,2048,4,128] rot 64", (q.numel() + k.numel()) * 2,
                 lambda: vlasr.rope_(q, k, head_dim=128, rotary_dim=64, seq_len=2048))
 
+    def rope_copy_floor():
+        # the floor for config 2's byte count at this launch size: one dense
+        # device copy (torch) moving as many bytes as the RoPE launch (the
+        # rotated halves of Q and K: 21 MB read, 21 MB written)
+        src = rnd((4 * 2048 * 20 * 64,))
+        dst = torch.empty_like(src)
+        return ("dense copy of the rotated halves' bytes (21 MB -> 21 MB)", 2 * src.numel() * 2,
+                lambda: dst.copy_(src))
+
     def _mel(chunks):
         from vlasr.synth import audio_chunks_device
         pcm = audio_chunks_device(chunks, 0, 7, dev)
@@ -472,6 +481,7 @@ def op_table(peak: float, only: str | None = None, iters_override: int | None = 
         ("add_rmsnorm", add_rmsnorm, 20, False),
         ("swiglu", swiglu, 20, False),
         ("rope", rope, 20, False),
+        ("rope_copy_floor", rope_copy_floor, 20, False),
         ("logmel", lambda: _mel(256), 5, False),
         ("logmel_1chunk", lambda: _mel(1), 20, False),
         ("decode_add_rmsnorm", decode_add_rmsnorm, 20, True),

@@ -206,12 +206,11 @@ class EncoderNormChain:
     GATHERS = ("copy", "nccl", "blocking")
 
     def __init__(self, shape: ChainShape, device, seed: int = 0, group=None, world: int = 1,
-                 rank: int = 0, total_chunks: int | None = None, gather: str = "nccl"):
-        """gather (world > 1): "nccl" - NCCL all_gather_into_tensor on a
-        side stream, overlapped with the next step; "copy" - copy-engine
-        pushes of each step's outputs into every rank's buffer, overlapped
-        with the next step (PeerPushGather); "blocking" - NCCL at the end of
-        each step."""
+                 rank: int = 0, total_chunks: int | None = None, gather: str = "copy"):
+        """gather (world > 1): "copy" - copy-engine pushes of each step's
+        outputs into every rank's buffer, overlapped with the next step
+        (PeerPushGather); "nccl" - NCCL all_gather_into_tensor on a side
+        stream, overlapped; "blocking" - NCCL at the end of each step."""
         if gather not in self.GATHERS:
             raise ValueError(f"gather must be one of {self.GATHERS}")
         self.shape = shape
