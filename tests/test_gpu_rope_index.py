@@ -253,3 +253,34 @@ def test_rope_kv_append_matches_separate_ops(dev):
         np.testing.assert_array_equal(_bits(a), _bits(b))
     eq, ek = oracle.rope(q, k, pos, 128, 64, 10000.0, "bf16")
     assert normwise(to_np(q1), eq) <= TOL["bf16"] and normwise(to_np(k1), ek) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("dtype,tokens,nq,nk,hd,rot", [
+    ("bf16", 1001, 16, 4, 128, 64),    # config-2 heads, partial last token group
+    ("f32", 3000, 20, 20, 64, 32),     # encoder heads, fp32 (2 vectors per half)
+    ("f16", 700, 16, 4, 128, 128),     # full rotary (8 vectors per half)
+    ("f32", 400, 16, 4, 128, 128),     # fp32 full rotary (16 vectors per half)
+    ("bf16", 333, 3, 1, 64, 64),       # few heads: several tokens per block group
+])
+def test_rope_inplace_matches_fused_append_at_stream_sizes(dev, dtype, tokens, nq, nk, hd, rot):
+    """vl_rope_inplace and vl_rope_kv_append at prefill-like token counts
+    (persistent warps, several tokens each, partial last round) must give
+    the same bits for q and k, and match the oracle."""
+    rng = np.random.default_rng(tokens + rot)
+    q, k = _qk(tokens, nq, nk, hd, dtype, seed=tokens)
+    v = oracle.round_to(rng.normal(0, 1, (tokens, nk, hd)), dtype)
+    pos = (rng.integers(0, 4096, tokens)).astype(np.int32)
+    td = torch_dtype(dtype)
+    q1, k1 = from_np(q, td, dev), from_np(k, td, dev)
+    pos_t = torch.from_numpy(pos).to(dev)
+    vlasr.rope_(q1, k1, head_dim=hd, rotary_dim=rot, positions=pos_t)
+    q2, k2, v2 = from_np(q, td, dev), from_np(k, td, dev), from_np(v, td, dev)
+    kc = torch.zeros(tokens, nk, hd, dtype=td, device=dev)
+    vc = torch.zeros_like(kc)
+    slot = torch.arange(tokens, dtype=torch.int64, device=dev)
+    vlasr.rope_kv_append(q2, k2, v2, kc, vc, pos_t, slot, head_dim=hd, rotary_dim=rot)
+    np.testing.assert_array_equal(_bits(q1), _bits(q2))
+    np.testing.assert_array_equal(_bits(k1), _bits(k2))
+    eq, ek = oracle.rope(q, k, pos, hd, rot, 10000.0, dtype)
+    assert normwise(to_np(q1), eq) <= TOL[dtype] and normwise(to_np(k1), ek) <= TOL[dtype]
+    np.testing.assert_array_equal(to_np(q1)[..., rot:], q[..., rot:])
