@@ -14,12 +14,13 @@
 //     twiddles, stage 2 = 20 DFT-20s (each DFT-20 a prime-factor 4 x 5 in
 //     registers, in packed fp32x2 arithmetic: one instruction per complex
 //     add/fma)
-//   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry
+//   |X_a|^2, |X_b|^2 from the packed spectrum's conjugate symmetry, in
+//     registers: the stage-2 lanes of k1 and 20 - k1 are neighbours and swap
+//     the mirror half of their outputs with one shuffle per bin
 //   sparse Slaney projection (394 nonzeros instead of 201 x 128 dense),
 //     one task per (frame, run of mel bins) with runs of equal cost
 //   log10(max(., 1e-10)) -> out, tile max -> workspace
-// The stage-1 transpose, the packed spectrum and the power spectra share one
-// 53 KB region; with the per-pair samples (prefetched for the next tile) and
+// The stage-1 transpose and the power spectra share one 53 KB region; with the per-pair samples (prefetched for the next tile) and
 // the tables a tile takes ~93 KB, two tiles per SM.  A second, light
 // kernel folds the tile maxima of each chunk and applies max(x, max-8) then
 // (x+4)/4 in place.  Chunks are processed in batches whose log-mel (1.5 MB
@@ -63,9 +64,6 @@ constexpr int kBins = 201;
 constexpr int kMel = 128;
 constexpr int kThreads = kPairs * 20;      // 320: one FFT task per thread, 10 warps
 constexpr int kTRow = 21;                  // padded row (complex) of the stage-1 transpose
-// padded row (complex) of the packed spectrum: two pairs sharing a warp then
-// start 8 banks apart, the fewest wavefronts for their 8-byte accesses
-constexpr int kZRow = 404;
 constexpr int kNormSlices = 16;            // normalise blocks per chunk
 constexpr int kBatchChunks = 32;           // chunks per L2-resident batch
 constexpr int kMaxTilesPerChunk = 125;     // capacity per chunk of the no-alloc scratch
@@ -74,12 +72,11 @@ static_assert(VL_MEL_GROUPS == kThreads / 32, "one mel-bin run per warp");
 
 struct MelSmem {
   float samples[kPairs * kPairStride];     // next tile's samples per pair, filled by cp.async
-  // stage-1 output t[p][k1][n2] -> packed spectra z[p][k] -> power spectra
-  // p[frame][bin]; each stage reads the previous one into registers and
-  // passes a barrier before writing the next.
+  // stage-1 output t[p][slot][n2] -> power spectra p[frame][bin]; stage 2
+  // reads the first into registers and passes a barrier before writing the
+  // second.
   union {
     float2 t[kPairs][20][kTRow];
-    float2 z[kPairs][kZRow];
     float p[kTileFrames][kBins];
   } u;
   float window[400];
@@ -185,6 +182,18 @@ __device__ __forceinline__ void dft20(c2 (&x)[20]) {
   }
 }
 
+// Stage-1 rows in mirror-pair order: slot 2m holds k1 = m and slot 2m + 1
+// holds k1 = 20 - m (m = 1..9); slots 0 and 1 hold k1 = 0 and 10, each its
+// own mirror.
+__device__ __forceinline__ constexpr int mirror_slot(int k1) {
+  return k1 == 0 ? 0 : (k1 == 10 ? 1 : (k1 < 10 ? 2 * k1 : 2 * (20 - k1) + 1));
+}
+__device__ __forceinline__ int slot_k1(int slot) {
+  const int m = slot >> 1;
+  if (slot == 1) return 10;
+  return (slot & 1) ? 20 - m : m;
+}
+
 __device__ __forceinline__ int reflect(int j) {
   if (j < 0) return -j;
   if (j >= kChunkSamples) return 2 * kChunkSamples - 2 - j;
@@ -256,46 +265,48 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int k1 = 0; k1 < 20; ++k1) {
       const float2 tw = sm.tw[k1][lane20];
-      *reinterpret_cast<unsigned long long*>(&sm.u.t[p][k1][lane20]) =
+      *reinterpret_cast<unsigned long long*>(&sm.u.t[p][mirror_slot(k1)][lane20]) =
           cmul_conj(x[k1], tw.x, tw.y).v;
     }
     __syncthreads();
 
-    // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2]
+    // ---- stage 2: per (pair, k1) DFT-20 over n2 -> Z[k1 + 20 k2].  Slot
+    // lane20 of the pair holds row k1 = slot_k1(lane20), so the lanes of a
+    // mirror pair (k1, 20 - k1) are neighbours (lane ^ 1, same warp).
 #pragma unroll
     for (int n2 = 0; n2 < 20; ++n2)
       x[n2].v = *reinterpret_cast<const unsigned long long*>(&sm.u.t[p][lane20][n2]);
-    __syncthreads();  // stage-1 output consumed: the region now takes Z
+    __syncthreads();  // stage-1 output consumed: the region now takes the power spectra
     dft20(x);
-#pragma unroll
-    for (int k2 = 0; k2 < 20; ++k2)
-      *reinterpret_cast<unsigned long long*>(&sm.u.z[p][lane20 + 20 * k2]) = x[k2].v;
-    __syncthreads();
 
-    // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i,
-    // all of this thread's bins into registers, then (the power spectra
-    // overwrite the spectrum) a barrier before they are stored
-    constexpr int kBinSteps = (kBins + 19) / 20;  // 11
-    float pa[kBinSteps], pb[kBinSteps];
+    // ---- power: X_a = (Z[k] + conj Z[400-k]) / 2, X_b = (Z[k] - conj Z[400-k]) / 2i.
+    // This lane holds Z[k1 + 20 k2]; the mirror Z[400 - k1 - 20 k2] is
+    // Z[k1' + 20 (19 - k2)] of the neighbour lane (k1' = 20 - k1), or of
+    // this lane itself when k1 is 0 (Z[20 ((20 - k2) mod 20)]) or 10
+    // (Z[10 + 20 (19 - k2)]).  Bins k1 + 20 k2 <= 200: k2 = 0..9, and for
+    // k1 = 0 also k2 = 10 (bin 200, its own mirror).
+    {
+      const int k1 = slot_k1(lane20);
+      const bool self = k1 == 0 || k1 == 10;
+      float* pa_row = sm.u.p[2 * p];
+      float* pb_row = sm.u.p[2 * p + 1];
 #pragma unroll
-    for (int i = 0; i < kBinSteps; ++i) {
-      const int k = lane20 + 20 * i;
-      if (k < kBins) {
-        const float2 a = sm.u.z[p][k];
-        const float2 b = sm.u.z[p][k == 0 ? 0 : 400 - k];
+      for (int k2 = 0; k2 < 10; ++k2) {
+        c2 m;
+        m.v = __shfl_xor_sync(0xffffffffu, x[19 - k2].v, 1);
+        if (self) m = k1 == 0 ? x[(20 - k2) % 20] : x[19 - k2];
+        const float2 a = split(x[k2]), b = split(m);
         const float ar = a.x + b.x, ai = a.y - b.y;
         const float br = a.x - b.x, bi = a.y + b.y;
-        pa[i] = (ar * ar + ai * ai) * 0.25f;
-        pb[i] = (br * br + bi * bi) * 0.25f;
+        pa_row[k1 + 20 * k2] = (ar * ar + ai * ai) * 0.25f;
+        pb_row[k1 + 20 * k2] = (br * br + bi * bi) * 0.25f;
       }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kBinSteps; ++i) {
-      const int k = lane20 + 20 * i;
-      if (k < kBins) {
-        sm.u.p[2 * p][k] = pa[i];
-        sm.u.p[2 * p + 1][k] = pb[i];
+      if (k1 == 0) {  // bin 200: Z[200] is its own mirror
+        const float2 a = split(x[10]), b = a;
+        const float ar = a.x + b.x, ai = a.y - b.y;
+        const float br = a.x - b.x, bi = a.y + b.y;
+        pa_row[200] = (ar * ar + ai * ai) * 0.25f;
+        pb_row[200] = (br * br + bi * bi) * 0.25f;
       }
     }
     __syncthreads();
