@@ -1317,7 +1317,8 @@ def main() -> None:
                "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
                "groups": len(host_group_bounds(shape.chunks, groups)),
-               "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers)",
+               "api": "vlasr.pipeline.EncoderNormChain.step_host (pinned host buffers; each "
+                      "chunk group's mel + layers replayed as one CUDA graph)",
                "breakdown": e2e_breakdown(trace, h2d, d2h, world)}
         del pcm_host, mel_host, y_host, pcm_dev
 

@@ -251,6 +251,8 @@ class EncoderNormChain:
         self.comm = None
         self.peers = None
         self.gather_done = [None, None]
+        # step_host: one CUDA graph per (chunk group, output buffer, PCM buffer)
+        self._group_graphs: dict[tuple[int, int, int, int], torch.cuda.CUDAGraph] = {}
         if world > 1:
             self.y_all = torch.empty((self.total_chunks * s.frames, s.hidden), device=self.device,
                                      dtype=bf)
@@ -358,20 +360,62 @@ class EncoderNormChain:
         self._end_step(timer)
 
     # -- host-buffer path -----------------------------------------------------
+    def _run_group(self, pcm_dev: torch.Tensor, c0: int, c1: int) -> None:
+        """Mel + every layer of chunks [c0, c1): 2 + 2 * layers launches."""
+        s = self.shape
+        self.run_mel(pcm_dev, c0, c1)
+        r0, r1 = c0 * s.frames, c1 * s.frames
+        for l in range(s.layers):
+            self.run_layer(l, r0, r1)
+
+    def _group_graph(self, pcm_dev: torch.Tensor, c0: int, c1: int) -> torch.cuda.CUDAGraph:
+        """The CUDA graph of _run_group(c0, c1) into the current output buffer,
+        captured on first use.  A replay is one launch on the host where the
+        group's own sequence is 66 library calls (2 + 2 x 32 layers): with
+        several chunk groups per step and one process per GPU, those calls
+        took as long as the GPU work itself, and the kernels waited for them."""
+        key = (c0, c1, self.cur, pcm_dev.data_ptr())
+        graph = self._group_graphs.get(key)
+        if graph is None:
+            ops.init(self.device)  # first-use set-up (tables, attributes) outside the capture
+            keep = self.cur
+            # both output buffers at once when they alternate, so that no
+            # later step captures (a capture synchronises the device)
+            for buf in range(len(self.y_bufs)):
+                self.cur = buf
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._run_group(pcm_dev, c0, c1)
+                self._group_graphs[(c0, c1, buf, pcm_dev.data_ptr())] = g
+            self.cur = keep
+            graph = self._group_graphs[key]
+        return graph
+
+    def release_graphs(self) -> None:
+        """Drop step_host's captured group graphs."""
+        self._group_graphs.clear()
+
     def step_host(self, pcm_host: torch.Tensor, mel_host: torch.Tensor, y_host: torch.Tensor,
-                  pcm_dev: torch.Tensor, groups: int = 4, trace: list | None = None) -> None:
+                  pcm_dev: torch.Tensor, groups: int = 4, trace: list | None = None,
+                  graphs: bool = True) -> None:
         """Host PCM [chunks, 480000] -> host mel [chunks,128,3000] and host
         encoder-norm outputs [chunks*frames, hidden] (pinned buffers).
 
         Chunk groups flow through three streams: group g+1's PCM uploads while
-        group g computes and group g-1's results download.  With `trace` (a
-        list), (kind, start, end) CUDA event pairs are appended for every
-        upload ("h2d"), group computation ("compute") and download ("d2h")."""
+        group g computes and group g-1's results download.  With `graphs`
+        (default), each group's computation is a CUDA graph replay, captured
+        on the first call with these groups (for both output buffers when
+        sharded); that call therefore synchronises the device and must not
+        itself run inside a capture.  With `trace` (a list), (kind,
+        start, end) CUDA event pairs are appended for every upload ("h2d"),
+        group computation ("compute") and download ("d2h")."""
         s = self.shape
+        bounds = host_group_bounds(s.chunks, groups)
+        group_graphs = [self._group_graph(pcm_dev, c0, c1) for c0, c1 in bounds] if graphs \
+            else None
         cur = torch.cuda.current_stream(self.device)
         up = torch.cuda.Stream(self.device)
         down = torch.cuda.Stream(self.device)
-        bounds = host_group_bounds(s.chunks, groups)
 
         def mark(stream):
             if trace is None:
@@ -392,13 +436,14 @@ class EncoderNormChain:
                 uploaded.append(ev)
                 if trace is not None:
                     trace.append(("h2d", a, ev))
-        for (c0, c1), ev in zip(bounds, uploaded):
+        for g, ((c0, c1), ev) in enumerate(zip(bounds, uploaded)):
             cur.wait_event(ev)
             a = mark(cur)
-            self.run_mel(pcm_dev, c0, c1)
+            if group_graphs is not None:
+                group_graphs[g].replay()
+            else:
+                self._run_group(pcm_dev, c0, c1)
             r0, r1 = c0 * s.frames, c1 * s.frames
-            for l in range(s.layers):
-                self.run_layer(l, r0, r1)
             done = torch.cuda.Event(enable_timing=trace is not None)
             done.record(cur)
             if trace is not None:
