@@ -484,16 +484,21 @@ VL_EXPORT int vl_decode_attention(const void* q, const void* k, const void* v,
  * Requires k % 512 == 0, n % 16 == 0 (n % 32 for SWIGLU), x / w / y and
  * norm_weight 16-byte aligned with row strides that are multiples of 8 elements, x not
  * overlapping y.  f16 / bf16.  No allocation, no synchronisation.
- * flags: 0 or VL_LAUNCH_PDL.
- * Kernels: from 17 rows, when the output columns (n, or n/2 for SWIGLU)
- * are a multiple of 128, the 5th-generation tensor cores compute it
+ * flags: VL_LAUNCH_PDL and / or VL_LINEAR_TCGEN05.
+ * Kernels: by default a tensor-core kernel of the previous generation
+ * (mma.sync), which spreads a few-row weight stream over many SMs.  With
+ * VL_LINEAR_TCGEN05, when the output columns (n, or n/2 for SWIGLU) are a
+ * multiple of 128, the 5th-generation tensor cores compute it instead
  * (tcgen05.mma with the accumulator in tensor memory, weights streamed by
  * TMA, K split over a thread-block cluster whose partial sums meet in
- * distributed shared memory); up to 16 rows and for other shapes a
- * tensor-core kernel of the previous generation (mma.sync), which spreads a
- * few-row weight stream over more SMs.  Both keep the rounding points
- * above; their fp32 summation orders differ, each is deterministic.
+ * distributed shared memory); other shapes ignore the flag.  On a B200 the
+ * tcgen05 kernel measured slower per launch than the default at every row
+ * count (its split-K clusters reach at most 15 x 8 CTAs, and each CTA's
+ * prologue, reduction and epilogue are serial latencies), so it is opt-in.
+ * Both keep the rounding points above; their fp32 summation orders differ,
+ * each is deterministic.
  */
+#define VL_LINEAR_TCGEN05 2
 #define VL_LINEAR_STORE 0
 #define VL_LINEAR_SWIGLU 1
 #define VL_LINEAR_RESIDUAL 2

@@ -197,6 +197,8 @@ def test_decode_linear_rejects(lib):
     assert call(so=FAKE * 4) == 2 and "RESIDUAL" in _err(lib)
     assert call(y=FAKE) == 2 and "overlaps" in _err(lib)
     assert call(flags=4) == 2 and "flags" in _err(lib)
+    # VL_LAUNCH_PDL | VL_LINEAR_TCGEN05 are accepted (the next check fails instead)
+    assert call(flags=3, rows=65) == 2 and "rows" in _err(lib)
     assert call(g=FAKE * 3 + 4, ssq=FAKE * 4, parts=128) == 2 and "norm_weight" in _err(lib)
 
 

@@ -2,7 +2,9 @@
 reference of the same math with the reference's rounding points
 (native/asr/src/decoder.cu: `gemm` outputs rounded to the storage type,
 rmsnorm_kernel, residual_add_kernel, silu_mul_kernel), for every epilogue,
-with and without the RMSNorm prologue, at 1..64 token rows."""
+with and without the RMSNorm prologue, at 1..64 token rows - every test
+twice: the default (mma.sync) kernel and the opt-in tcgen05 kernel
+(VL_LINEAR_TCGEN05)."""
 
 from __future__ import annotations
 
@@ -16,6 +18,19 @@ from helpers import TOL, normwise, to_np
 pytestmark = pytest.mark.gpu
 
 DT = [(torch.bfloat16, "bf16"), (torch.float16, "f16")]
+_TC = [False]
+
+
+@pytest.fixture(params=[False, True], ids=["mma_sync", "tcgen05"], autouse=True)
+def _kernel(request):
+    _TC[0] = request.param
+    yield
+    _TC[0] = False
+
+
+def _lin(*args, **kwargs):
+    """vl_decode_linear through the kernel this test instance exercises."""
+    return vlasr.decode_linear(*args, tcgen05=_TC[0], **kwargs)
 
 
 def _rand(shape, dev, dtype, seed, std=1.0):
@@ -37,7 +52,7 @@ def _norm_ref(h, gamma, ssq_rows, k, dtype, eps=1e-5):
 def test_store(dev, dtype, name, rows):
     x = _rand((rows, 2048), dev, dtype, rows)
     w = _rand((3072, 2048), dev, dtype, 100 + rows, 2048 ** -0.5)
-    y = vlasr.decode_linear(x, w)
+    y = _lin(x, w)
     ref = _r(x.float() @ w.float().t(), dtype)
     torch.cuda.synchronize()
     assert normwise(to_np(y), to_np(ref)) <= TOL[name]
@@ -48,7 +63,7 @@ def test_swiglu(dev, dtype, name):
     rows, k, ffn = 16, 2048, 6144
     x = _rand((rows, k), dev, dtype, 1)
     w = _rand((2 * ffn, k), dev, dtype, 2, k ** -0.5 * 2)
-    y = vlasr.decode_linear(x, w, epilogue="swiglu")
+    y = _lin(x, w, epilogue="swiglu")
     gu = x.float() @ w.float().t()
     g, u = _r(gu[:, :ffn], dtype), _r(gu[:, ffn:], dtype)
     ref = _r(g / (1 + torch.exp(-g)) * u, dtype)
@@ -70,13 +85,13 @@ def test_residual_and_norm_chain(dev, dtype, name):
     wq = _rand((3072, hid), dev, dtype, 7, hid ** -0.5)
     h_ref = _r(h.float() + _r(m.float() @ wd.float().t(), dtype), dtype)
     ssq = torch.empty(hid // 16, rows, dtype=torch.float32, device=dev)
-    vlasr.decode_linear(m, wd, epilogue="residual", out=h, ssq_out=ssq)
+    _lin(m, wd, epilogue="residual", out=h, ssq_out=ssq)
     torch.cuda.synchronize()
     assert normwise(to_np(h), to_np(h_ref)) <= TOL[name]
     # partial sums are exact sums of squares of the new residual values
     hs = h.float().view(rows, hid // 16, 16)
     assert torch.allclose(ssq, (hs * hs).sum(-1).t(), rtol=1e-5, atol=1e-5)
-    q = vlasr.decode_linear(h, wq, norm_weight=gamma, ssq_in=ssq)
+    q = _lin(h, wq, norm_weight=gamma, ssq_in=ssq)
     xn = _norm_ref(h, gamma, (h.float() ** 2).sum(-1), hid, dtype)
     ref = _r(xn @ wq.float().t(), dtype)
     torch.cuda.synchronize()
@@ -91,9 +106,9 @@ def test_norm_prologue_matches_add_rmsnorm(dev):
     w = _rand((12288, hid), dev, torch.bfloat16, 10, hid ** -0.5)
     hs = h.float().view(rows, hid // 16, 16)
     ssq = (hs * hs).sum(-1).t().contiguous()
-    fused = vlasr.decode_linear(h, w, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
+    fused = _lin(h, w, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
     xn = vlasr.add_rmsnorm(h.clone(), None, gamma)
-    plain = vlasr.decode_linear(xn, w, epilogue="swiglu")
+    plain = _lin(xn, w, epilogue="swiglu")
     torch.cuda.synchronize()
     same = (fused == plain).float().mean().item()
     assert normwise(to_np(fused), to_np(plain)) <= 1e-2 and same > 0.9, same
@@ -104,7 +119,7 @@ def test_row_stride_and_lm_head_width(dev):
     buf = _rand((rows, 3 * hid), dev, torch.bfloat16, 11)
     x = buf[:, hid:2 * hid]
     w = _rand((vocab, hid), dev, torch.bfloat16, 12, hid ** -0.5)
-    y = vlasr.decode_linear(x, w)
+    y = _lin(x, w)
     ref = _r(x.float() @ w.float().t(), torch.bfloat16)
     torch.cuda.synchronize()
     assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]
@@ -115,8 +130,8 @@ def test_row_stride_and_lm_head_width(dev):
 def test_deterministic(dev):
     x = _rand((16, 2048), dev, torch.bfloat16, 13)
     w = _rand((2048, 2048), dev, torch.bfloat16, 14, 2048 ** -0.5)
-    a = vlasr.decode_linear(x, w)
-    b = vlasr.decode_linear(x, w)
+    a = _lin(x, w)
+    b = _lin(x, w)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
 
@@ -125,9 +140,9 @@ def test_rejects(dev):
     x = _rand((65, 2048), dev, torch.bfloat16, 15)
     w = _rand((2048, 2048), dev, torch.bfloat16, 16)
     with pytest.raises(vlasr.VlasrInputError, match="rows"):
-        vlasr.decode_linear(x, w)
+        _lin(x, w)
     with pytest.raises(vlasr.VlasrInputError, match="in place"):
-        vlasr.decode_linear(x[:4], w, epilogue="residual")
+        _lin(x[:4], w, epilogue="residual")
 
 
 def test_pdl_chain_is_bit_identical(dev):
@@ -158,13 +173,13 @@ def test_pdl_chain_is_bit_identical(dev):
                 "m": torch.empty(rows, ffn, dtype=torch.bfloat16, device=dev)}
 
     def chain(st, pdl):
-        vlasr.decode_linear(m0, w_d, epilogue="residual", out=st["h"], ssq_out=st["sa"], pdl=pdl)
-        qkv = vlasr.decode_linear(st["h"], w_qkv, norm_weight=g1, ssq_in=st["sa"], pdl=pdl)
+        _lin(m0, w_d, epilogue="residual", out=st["h"], ssq_out=st["sa"], pdl=pdl)
+        qkv = _lin(st["h"], w_qkv, norm_weight=g1, ssq_in=st["sa"], pdl=pdl)
         a = vlasr.decode_attention(qkv[:, :2048], st["kc"], st["vc"], pos, start, n_kv_heads=4,
                                    head_dim=128, max_seq_len=slots, k=qkv[:, 2048:2560],
                                    v=qkv[:, 2560:], rotary_dim=128, workspace=st["ws"], pdl=pdl)
-        vlasr.decode_linear(a, w_o, epilogue="residual", out=st["h"], ssq_out=st["sb"], pdl=pdl)
-        vlasr.decode_linear(st["h"], w_gu, norm_weight=g2, ssq_in=st["sb"], epilogue="swiglu",
+        _lin(a, w_o, epilogue="residual", out=st["h"], ssq_out=st["sb"], pdl=pdl)
+        _lin(st["h"], w_gu, norm_weight=g2, ssq_in=st["sb"], epilogue="swiglu",
                             out=st["m"], pdl=pdl)
 
     plain, eager = state(), state()
@@ -190,22 +205,22 @@ def test_pdl_chain_is_bit_identical(dev):
                                         ("residual", 2064)])
 def test_shapes_outside_the_tensor_core_tiles(dev, epilogue, n):
     """Output widths that are not a multiple of 128 columns take the
-    mma.sync kernel; same references."""
+    mma.sync kernel (the tcgen05 flag is ignored there); same references."""
     rows, k = 9, 2048
     x = _rand((rows, k), dev, torch.bfloat16, 40 + n)
     w = _rand((n, k), dev, torch.bfloat16, 41 + n, k ** -0.5)
     acc = x.float() @ w.float().t()
     if epilogue == "store":
-        y = vlasr.decode_linear(x, w)
+        y = _lin(x, w)
         ref = _r(acc, torch.bfloat16)
     elif epilogue == "swiglu":
-        y = vlasr.decode_linear(x, w, epilogue="swiglu")
+        y = _lin(x, w, epilogue="swiglu")
         g, u = _r(acc[:, :n // 2], torch.bfloat16), _r(acc[:, n // 2:], torch.bfloat16)
         ref = _r(g / (1 + torch.exp(-g)) * u, torch.bfloat16)
     else:
         h = _rand((rows, n), dev, torch.bfloat16, 42)
         ref = _r(h.float() + _r(acc, torch.bfloat16), torch.bfloat16)
-        y = vlasr.decode_linear(x, w, epilogue="residual", out=h)
+        y = _lin(x, w, epilogue="residual", out=h)
     torch.cuda.synchronize()
     assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]
 
@@ -222,14 +237,14 @@ def test_tensor_core_row_paddings_all_epilogues(dev, rows):
     w_d = _rand((hid, ffn), dev, torch.bfloat16, 54, ffn ** -0.5)
     xs = x.float().view(rows, hid // 16, 16)
     ssq = (xs * xs).sum(-1).t().contiguous()
-    y = vlasr.decode_linear(x, w_gu, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
+    y = _lin(x, w_gu, norm_weight=gamma, ssq_in=ssq, epilogue="swiglu")
     xn = _norm_ref(x, gamma, (x.float() ** 2).sum(-1), hid, torch.bfloat16)
     gu = xn @ w_gu.float().t()
     g, u = _r(gu[:, :ffn], torch.bfloat16), _r(gu[:, ffn:], torch.bfloat16)
     ref = _r(g / (1 + torch.exp(-g)) * u, torch.bfloat16)
     h = x.clone()
     part = torch.empty(hid // 16, rows, dtype=torch.float32, device=dev)
-    vlasr.decode_linear(m, w_d, epilogue="residual", out=h, ssq_out=part)
+    _lin(m, w_d, epilogue="residual", out=h, ssq_out=part)
     h_ref = _r(x.float() + _r(m.float() @ w_d.float().t(), torch.bfloat16), torch.bfloat16)
     torch.cuda.synchronize()
     assert normwise(to_np(y), to_np(ref)) <= TOL["bf16"]

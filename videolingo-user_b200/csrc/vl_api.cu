@@ -617,7 +617,7 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
     return fail(VL_ERR_INVALID, "%s: null pointer", op);
   if (dtype != VL_F16 && dtype != VL_BF16)
     return fail(VL_ERR_INVALID, "%s: unsupported dtype %d (f16 or bf16)", op, dtype);
-  if ((flags & ~VL_LAUNCH_PDL) != 0)
+  if ((flags & ~(VL_LAUNCH_PDL | VL_LINEAR_TCGEN05)) != 0)
     return fail(VL_ERR_INVALID, "%s: unknown flags 0x%x", op, flags);
   if (epilogue != VL_LINEAR_STORE && epilogue != VL_LINEAR_SWIGLU &&
       epilogue != VL_LINEAR_RESIDUAL)
@@ -664,6 +664,7 @@ int vl_decode_linear(const void* x, int64_t x_row_stride, const void* norm_weigh
   a.rows = rows;
   a.epilogue = epilogue;
   return exec_status(vl::launch_decode_linear(a, dtype, (flags & VL_LAUNCH_PDL) != 0,
+                                              (flags & VL_LINEAR_TCGEN05) != 0,
                                               static_cast<cudaStream_t>(stream)),
                      op);
 }

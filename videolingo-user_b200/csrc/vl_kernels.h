@@ -115,10 +115,10 @@ struct LinearArgs {
   int64_t rows;
   int epilogue;              // VL_LINEAR_STORE / _SWIGLU / _RESIDUAL
 };
-cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, bool pdl,
+cudaError_t launch_decode_linear(const LinearArgs& args, int dtype, bool pdl, bool tcgen05,
                                  cudaStream_t stream);
 // The tensor-core (tcgen05 / TMA / TMEM) form of the same op (vl_linear_tc.cu),
-// used by launch_decode_linear for the shapes it supports.
+// used by launch_decode_linear on request for the shapes it supports.
 bool decode_linear_tc_supported(const LinearArgs& args, int dtype);
 cudaError_t launch_decode_linear_tc(const LinearArgs& args, int dtype, bool pdl,
                                     cudaStream_t stream);

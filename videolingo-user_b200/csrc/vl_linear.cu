@@ -45,7 +45,6 @@ constexpr int lin_warps() { return EPI == VL_LINEAR_SWIGLU ? 4 : 8; }
 #define VL_LINEAR_STAGES 3
 #endif
 constexpr int kKc = 64;       // k per ring stage
-constexpr int kTcMinRows = 17;  // from this many rows the tcgen05 kernel takes the call
 constexpr int kCols = 16;     // output columns per CTA
 constexpr size_t kLinRingBudget = 200 * 1024;
 
@@ -390,13 +389,14 @@ cudaError_t linear_typed(const LinearArgs& a, bool pdl, cudaStream_t stream) {
 
 }  // namespace
 
-cudaError_t launch_decode_linear(const LinearArgs& a, int dtype, bool pdl, cudaStream_t stream) {
+cudaError_t launch_decode_linear(const LinearArgs& a, int dtype, bool pdl, bool tcgen05,
+                                 cudaStream_t stream) {
   if (a.rows == 0) return cudaSuccess;
-  // More than 16 rows with output columns in tiles of 128: the tcgen05
-  // kernel (vl_linear_tc.cu), which beats this one from 17 to 64 rows; up to
-  // 16 rows this kernel streams the weights over more SMs and is faster
-  // (the tcgen05 kernel's split-K clusters are limited to 15 of 8 CTAs).
-  if (a.rows > kTcMinRows - 1 && decode_linear_tc_supported(a, dtype))
+  // On request, output columns in tiles of 128: the tcgen05 kernel
+  // (vl_linear_tc.cu).  This kernel is the default: it streams a few-row
+  // weight matrix over more SMs and measured faster at every row count (the
+  // tcgen05 kernel's split-K clusters are limited to 15 of 8 CTAs).
+  if (tcgen05 && decode_linear_tc_supported(a, dtype))
     return launch_decode_linear_tc(a, dtype, pdl, stream);
   if (dtype == kDtypeBF16) return linear_typed<__nv_bfloat16>(a, pdl, stream);
   if (dtype == kDtypeF16) return linear_typed<__half>(a, pdl, stream);

@@ -48,9 +48,9 @@ EOS_IDS = (59246, 59253, 59255)
 AUDIO_TOKEN_ID = 59260
 AUDIO_TOKENS_PER_CHUNK = 375
 # Decode steps of up to this many chunks run the fused layers through
-# vl_decode_linear (its mma.sync kernel); larger batches run cuBLAS GEMMs,
-# which measured faster per launch than either kernel of vl_decode_linear
-# from 17 rows up.
+# vl_decode_linear (its default mma.sync kernel); larger batches run cuBLAS
+# GEMMs, which measured faster per launch than either kernel of
+# vl_decode_linear from 17 rows up.
 FUSED_MAX_ROWS = 16
 
 

@@ -470,13 +470,15 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
 
 LINEAR_EPILOGUES = {"store": 0, "swiglu": 1, "residual": 2}
 LAUNCH_PDL = 1        # VL_LAUNCH_PDL
+LINEAR_TCGEN05 = 2    # VL_LINEAR_TCGEN05
 LINEAR_MAX_ROWS = 64
 
 
 def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
                   out: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
                   ssq_in: torch.Tensor | None = None, eps: float = 1e-5,
-                  ssq_out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+                  ssq_out: torch.Tensor | None = None, pdl: bool = False,
+                  tcgen05: bool = False) -> torch.Tensor:
     """y = x W^T for at most 64 token rows (vl_decode_linear).
 
     x [rows, k] (a row stride is allowed), w [n, k].  epilogue "store" -> out
@@ -486,7 +488,9 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
     norm_weight + ssq_in (float32 [parts, rows], such partial sums) apply
     the RMSNorm prologue to x.  pdl=True launches it as a programmatic
     dependent of the previous kernel on the stream (VL_LAUNCH_PDL): that
-    kernel must not write w or norm_weight."""
+    kernel must not write w or norm_weight.  tcgen05=True asks for the
+    5th-generation tensor-core kernel (VL_LINEAR_TCGEN05; output columns in
+    multiples of 128, otherwise ignored); the default kernel is faster."""
     if epilogue not in LINEAR_EPILOGUES:
         raise VlasrInputError(f"epilogue must be one of {sorted(LINEAR_EPILOGUES)}")
     _cuda(x, "x")
@@ -524,7 +528,8 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "store",
     check(_lib.load().vl_decode_linear(
         _ptr(x), x.stride(0), _ptr(norm_weight), _ptr(ssq_in), parts, float(eps), _ptr(w), n, k,
         _ptr(out), out.stride(0), _ptr(ssq_out), rows, LINEAR_EPILOGUES[epilogue],
-        _dtype_code(x), LAUNCH_PDL if pdl else 0, _stream(x)), "vl_decode_linear")
+        _dtype_code(x), (LAUNCH_PDL if pdl else 0) | (LINEAR_TCGEN05 if tcgen05 else 0),
+        _stream(x)), "vl_decode_linear")
     return out
 
 
