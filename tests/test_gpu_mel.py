@@ -64,16 +64,17 @@ def test_matches_reference_fp32_restatement(dev):
 
 
 def test_chunks_are_independent_across_batches(dev):
-    """35 chunks span two kernel batches; each chunk equals its own 1-chunk run."""
-    pcm = audio_chunks(35, seed=13)
+    """67 chunks span two kernel batches (33 + 34); each chunk equals its own
+    1-chunk run."""
+    pcm = audio_chunks(67, seed=13)
     pcm[4] *= 0.01           # different chunk maxima
-    pcm[33] = 0.0            # silent chunk in the second batch
+    pcm[35] = 0.0            # silent chunk in the second batch
     many = _mel(dev, pcm)
-    for c in (0, 4, 31, 32, 33, 34):
+    for c in (0, 4, 32, 33, 35, 66):
         one = _mel(dev, pcm[c])
         np.testing.assert_array_equal(many[c], one[0])
-    exp = oracle.logmel_f64(pcm[[0, 32, 34]])
-    assert normwise(many[[0, 32, 34]], exp) <= 1e-5
+    exp = oracle.logmel_f64(pcm[[0, 33, 66]])
+    assert normwise(many[[0, 33, 66]], exp) <= 1e-5
 
 
 def test_silence_and_full_scale(dev):
