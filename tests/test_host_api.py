@@ -48,3 +48,23 @@ def test_pad_chunk_matches_reference_contract():
     assert y.shape == (480000,) and np.array_equal(y[:1000], x) and not y[1000:].any()
     with pytest.raises(ValueError):
         synth.pad_chunk(np.zeros(480001, np.float32))
+
+
+def test_chain_launch_count_matches_the_mel_batching():
+    """gpu_launches in the bench line: per step a tile and a normalise launch
+    per mel batch of at most 64 chunks, plus add+LN and GELU per layer."""
+    from vlasr.pipeline import MEL_BATCH_CHUNKS, ChainShape, EncoderNormChain
+
+    class _Shape:
+        pass
+
+    chain = _Shape()
+    for chunks, groups, want in ((256, 1, 2 * 4 + 64), (65, 1, 2 * 2 + 64), (64, 1, 2 + 64),
+                                 (32, 4, 2 * 4 + 64 * 4)):
+        chain.shape = ChainShape(chunks=chunks)
+        assert EncoderNormChain.launches_per_step(chain, groups) == want
+    import re
+    from pathlib import Path
+    src = (Path(__file__).resolve().parents[1] / "videolingo-user_b200" / "csrc" /
+           "vl_mel.cu").read_text()
+    assert int(re.search(r"kBatchChunks = (\d+);", src).group(1)) == MEL_BATCH_CHUNKS

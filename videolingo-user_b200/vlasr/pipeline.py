@@ -177,6 +177,9 @@ class PeerPushGather:
 
 
 EDGE_MAX_CHUNKS = 4
+# chunks per mel batch in vl_logmel (csrc/vl_mel.cu kBatchChunks): each batch
+# is one tile launch and one normalise launch
+MEL_BATCH_CHUNKS = 64
 
 
 def host_group_bounds(chunks: int, groups: int) -> list[tuple[int, int]]:
@@ -269,13 +272,14 @@ class EncoderNormChain:
 
     # -- launch sequences ---------------------------------------------------
     def launches_per_step(self, groups: int = 1) -> int:
-        """Kernels of this library launched by one step (mel: 2 per 32-chunk batch)."""
+        """Kernels of this library launched by one step (mel: a tile and a
+        normalise launch per batch of at most MEL_BATCH_CHUNKS chunks)."""
         per_group = math.ceil(self.shape.chunks / groups)
         mel = 0
         left = self.shape.chunks
         while left > 0:
             n = min(per_group, left)
-            mel += 2 * math.ceil(n / 32)
+            mel += 2 * math.ceil(n / MEL_BATCH_CHUNKS)
             left -= n
         return mel + 2 * self.shape.layers * groups
 
