@@ -19,9 +19,13 @@ SOURCES = sorted((ROOT / "videolingo-user_b200" / "vlasr").glob("*.py")) + [
     (ROOT / "tests").glob("*.py"))
 
 
+MODULE_ATTRS = {"__file__", "__name__", "__doc__", "__spec__", "__loader__", "__package__",
+                "__path__", "__builtins__"}
+
+
 def _module_names(table: symtable.SymbolTable) -> set[str]:
-    return {s.get_name() for s in table.get_symbols()
-            if s.is_assigned() or s.is_imported() or s.is_namespace()}
+    return MODULE_ATTRS | {s.get_name() for s in table.get_symbols()
+                           if s.is_assigned() or s.is_imported() or s.is_namespace()}
 
 
 def _unresolved(table: symtable.SymbolTable, module: set[str], path: str) -> list[str]:
